@@ -1,0 +1,135 @@
+// Host side of the grouped INT8/INT4 GEMV: shape checks, tile/stage selection and the
+// launch (optionally with programmatic dependent launch). The kernel is in gemv.cuh.
+#include <mutex>
+
+#include "gemv.cuh"
+#include "ops.h"
+
+namespace cb {
+
+namespace {
+
+using KernelFn = void (*)(GemvArgs);
+
+template <int WF, int MT, int RPW, int PRO, int EPI>
+KernelFn fn() {
+    return &qgemv_kernel<WF, MT, RPW, PRO, EPI>;
+}
+
+// (pro, epi) combinations used by the op API and the models
+constexpr int kCombos[][2] = {
+    {kProPreq, kEpiStore},         {kProQuant, kEpiStore},          {kProQuant, kEpiResidual},
+    {kProRmsNormQuant, kEpiStore}, {kProRmsNormQuant, kEpiGluSilu}, {kProRmsNormQuant, kEpiGluGelu},
+};
+constexpr int kNumCombos = sizeof(kCombos) / sizeof(kCombos[0]);
+
+int combo_index(int pro, int epi) {
+    for (int i = 0; i < kNumCombos; ++i)
+        if (kCombos[i][0] == pro && kCombos[i][1] == epi) return i;
+    return -1;
+}
+
+template <int WF, int MT, int RPW>
+KernelFn pick_combo(int ci) {
+    switch (ci) {
+        case 0: return fn<WF, MT, RPW, kProPreq, kEpiStore>();
+        case 1: return fn<WF, MT, RPW, kProQuant, kEpiStore>();
+        case 2: return fn<WF, MT, RPW, kProQuant, kEpiResidual>();
+        case 3: return fn<WF, MT, RPW, kProRmsNormQuant, kEpiStore>();
+        case 4: return fn<WF, MT, RPW, kProRmsNormQuant, kEpiGluSilu>();
+        case 5: return fn<WF, MT, RPW, kProRmsNormQuant, kEpiGluGelu>();
+    }
+    return nullptr;
+}
+template <int WF, int MT>
+KernelFn pick_rpw(int rpw, int ci) {
+    return rpw == 4 ? pick_combo<WF, MT, 4>(ci) : pick_combo<WF, MT, 1>(ci);
+}
+template <int WF>
+KernelFn pick_mt(int mt, int rpw, int ci) {
+    switch (mt) {
+        case 1: return pick_rpw<WF, 1>(rpw, ci);
+        case 2: return pick_rpw<WF, 2>(rpw, ci);
+        case 4: return pick_rpw<WF, 4>(rpw, ci);
+        default: return pick_rpw<WF, 8>(rpw, ci);
+    }
+}
+
+std::mutex g_attr_mu;
+bool g_attr_set[2][9][5][kNumCombos] = {};
+
+}  // namespace
+
+const char* gemv_check(const GemvCall& c) {
+    if (c.M < 1 || c.M > 8) return "gemv: M must be in [1, 8]";
+    if (c.N < 1 || c.K < 1 || c.G < 1) return "gemv: empty shape";
+    if (c.K % c.G) return "gemv: K must be a multiple of group_size";
+    if (!c.int4 && (c.G % 16 || c.G > 512)) return "gemv: INT8 group_size must be a multiple of 16 and <= 512";
+    if (c.int4 && (c.G % 32 || c.G > 1024)) return "gemv: INT4 group_size must be a multiple of 32 and <= 1024";
+    if ((reinterpret_cast<uintptr_t>(c.w) & 15) || (reinterpret_cast<uintptr_t>(c.ws) & 15))
+        return "gemv: weights and scales must be 16-byte aligned";
+    if ((c.epi == kEpiGluSilu || c.epi == kEpiGluGelu) && (c.N & 1)) return "gemv: GLU epilogue needs even N";
+    if (combo_index(c.pro, c.epi) < 0) return "gemv: unsupported prologue/epilogue combination";
+    const GemvLayout L = gemv_layout(c.int4, 8, 1, 2, c.pro, c.K, c.G);
+    if (L.total > 227 * 1024) return "gemv: K too large for the shared-memory tile";
+    return nullptr;
+}
+
+int launch_gemv(const GemvCall& c, cudaStream_t st) {
+    const int mt = c.M <= 1 ? 1 : c.M <= 2 ? 2 : c.M <= 4 ? 4 : 8;
+    const int tiles4 = (c.N + 31) / 32;
+    const int rpw = (tiles4 >= 2 * kNumSMs && mt * 4 <= 32) ? 4 : 1;
+    const int R = 8 * rpw;
+    const int ntiles = (c.N + R - 1) / R;
+    int S = 4;
+    GemvLayout L = gemv_layout(c.int4, mt, rpw, S, c.pro, c.K, c.G);
+    while (S > 2 && L.total > 112 * 1024) {
+        --S;
+        L = gemv_layout(c.int4, mt, rpw, S, c.pro, c.K, c.G);
+    }
+    if (L.total > 227 * 1024) return -1;
+    const int per_sm = L.total <= 112 * 1024 ? 2 : 1;
+    const int grid = ntiles < per_sm * kNumSMs ? ntiles : per_sm * kNumSMs;
+    const int ci = combo_index(c.pro, c.epi);
+    KernelFn f = c.int4 ? pick_mt<1>(mt, rpw, ci) : pick_mt<0>(mt, rpw, ci);
+    if (!f) return -1;
+    {
+        std::lock_guard<std::mutex> lk(g_attr_mu);
+        bool& done = g_attr_set[c.int4][mt][rpw][ci];
+        if (!done) {
+            if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+                return -1;
+            done = true;
+        }
+    }
+    GemvArgs a;
+    a.x = c.x;
+    a.norm_w = c.norm_w;
+    a.eps = c.eps;
+    a.aq = c.aq;
+    a.as = c.as;
+    a.w = c.w;
+    a.ws = c.ws;
+    a.out = c.out;
+    a.resid = c.resid;
+    a.aq_out = c.aq_out;
+    a.as_out = c.as_out;
+    a.M = c.M;
+    a.K = c.K;
+    a.N = c.N;
+    a.G = c.G;
+    a.S = S;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = c.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, f, a) == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace cb

@@ -1,0 +1,355 @@
+// Grouped INT8 / INT4 weight GEMV for small M (decode), sm_100a.
+//
+// Replaces cactus_matmul_int8 (kernel_gemm.cpp:128-327) and cactus_matmul_int4
+// (kernel_gemm.cpp:329-529) together with the activation quantization that
+// compute_matmul_node runs first (graph_ops_nn.cpp:35-66, 150-209).
+//
+// Arithmetic (bit-exact with the reference semantics):
+//   A_q[m,:] = sat8(rne(x[m,:] * (1 / s_m))),  s_m = max(absmax(x[m,:]) / 127, 1e-10)
+//   C[m,n]   = fp16( fma-chain_g( float(sum_{k in g} A_q[m,k] * B[n,k]), float(Bs[n,g]) ) * s_m )
+// with the group sums exact in int32 and the fp32 chain over groups in ascending g.
+//
+// Data path: weights are row-major [N, K] (int8) or [N, K/2] (int4, low nibble = even k)
+// with fp16 scales [N, K/G]. A CTA owns tiles of R = 8*RPW consecutive rows; each tile's
+// weight bytes and scales are contiguous in HBM and arrive in shared memory through one
+// 1-D TMA bulk copy each (cp.async.bulk, no multicast) into an S-stage mbarrier ring.
+// Weight copies are issued before griddepcontrol.wait, so under programmatic dependent
+// launch they stream while the producer of the activations is still finishing.
+#pragma once
+#include "common.cuh"
+
+namespace cb {
+
+enum class WFmt : int { I8 = 0, I4 = 1 };
+enum class Pro : int { PREQ = 0, QUANT = 1, RMSNORM_QUANT = 2 };
+enum class Epi : int { STORE = 0, RESIDUAL = 1, GLU_SILU = 2, GLU_GELU = 3 };
+
+struct GemvArgs {
+    const __half* x;       // QUANT / RMSNORM_QUANT: fp16 activations [M, K]
+    const __half* norm_w;  // RMSNORM_QUANT: [K]
+    float eps;
+    const int8_t* aq;  // PREQ: int8 activations [M, K]
+    const float* as;   // PREQ: per-row scales [M]
+    const void* w;     // [N, K] int8 or [N, K/2] uint8
+    const __half* ws;  // [N, K/G]
+    __half* out;       // STORE/RESIDUAL: [M, N]; GLU: [M, N/2]
+    const __half* resid;  // RESIDUAL: [M, N] (may alias out)
+    int8_t* aq_out;    // optional: block 0 writes the quantized activations here
+    float* as_out;     // optional
+    int M, K, N, G;
+    int S;  // pipeline stages (>= 2)
+};
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+
+struct GemvLayout {
+    int R, wrow, ng, stage_w, stage_s, stage_bytes, S, gpj, pairs;
+    int off_act, off_asum, off_as, off_xs, off_stage, off_bar, off_gs, off_out, total;
+};
+
+__host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline GemvLayout gemv_layout(int wf, int MT, int RPW, int S, int pro, int K, int G) {
+    GemvLayout L;
+    L.R = 8 * RPW;
+    L.wrow = wf == 0 ? K : K / 2;
+    L.ng = K / G;
+    L.stage_w = L.R * L.wrow;
+    L.stage_s = L.R * L.ng * 2;
+    L.stage_bytes = align_up(L.stage_w + align_up(L.stage_s, 16), 128);
+    L.S = S;
+    L.gpj = wf == 0 ? 512 / G : 1024 / G;  // groups covered by one 32-lane pass
+    if (L.gpj < 1) L.gpj = 1;
+    L.pairs = RPW * MT;
+    int off = 0;
+    L.off_act = off;   off += align_up(MT * K, 128);
+    L.off_asum = off;  off += align_up(MT * L.ng * 4, 128);
+    L.off_as = off;    off += align_up(MT * 4, 16) + 112;
+    L.off_xs = off;    off += (pro == 2) ? align_up(MT * K * 2, 128) : 0;
+    L.off_stage = off; off += S * L.stage_bytes;
+    L.off_bar = off;   off += align_up(S * 8, 16) + 16;
+    L.off_gs = off;    off += align_up(kGemvWarps * L.pairs * L.gpj * 4, 16) > 128 ? align_up(kGemvWarps * L.pairs * L.gpj * 4, 16) : 128;
+    off = align_up(off, 16);
+    L.off_out = off;   off += 2 * L.R * MT * 2;
+    L.total = align_up(off, 128);
+    return L;
+}
+
+// ------------------------------------------------------------------ prologue helpers
+// Bit-exact restatement of cactus_rms_norm_f16's reduction (kernel_attention.cpp:496-540):
+// 16 lane accumulators over 16-element tiles, an 8-element tail tile into lanes 0..7, the
+// fixed combine tree and a scalar tail. Runs on one warp; result broadcast to all lanes.
+__device__ __forceinline__ float rms_sumsq_warp(const __half* xs, int K) {
+    const int lane = threadIdx.x & 31;
+    float acc = 0.0f;
+    int i = 0;
+    const int tile_end = K >= 16 ? K - 16 + 1 : 0;
+    for (; i < tile_end; i += 16)
+        if (lane < 16) { float v = h2f(xs[i + lane]); acc = fmaf(v, v, acc); }
+    const int simd_end = K >= 8 ? K - 8 + 1 : 0;
+    if (i < simd_end) {
+        if (lane < 8) { float v = h2f(xs[i + lane]); acc = fmaf(v, v, acc); }
+        i += 8;
+    }
+    float a4 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 4);
+    float a8 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 8);
+    float a12 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 12);
+    float a0 = __shfl_sync(0xffffffffu, acc, lane & 3);
+    float t = __fadd_rn(__fadd_rn(__fadd_rn(a0, a4), a8), a12);
+    float t0 = __shfl_sync(0xffffffffu, t, 0), t1 = __shfl_sync(0xffffffffu, t, 1);
+    float t2 = __shfl_sync(0xffffffffu, t, 2), t3 = __shfl_sync(0xffffffffu, t, 3);
+    float ss = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
+    for (; i < K; ++i) { float v = h2f(xs[i]); ss = fmaf(v, v, ss); }
+    return ss;
+}
+
+// Quantize one fp16 value with the reference's activation rule; `vec` selects the
+// NEON vector path (RNE after clamping) versus the scalar tail (round half away).
+__device__ __forceinline__ int8_t quant_act(float v, float inv, bool vec) {
+    float s = __fmul_rn(v, inv);
+    s = fmaxf(fminf(s, 127.0f), -128.0f);
+    return vec ? (int8_t)sat8(cvt_rne_sat(s)) : (int8_t)(int)roundf(s);
+}
+
+template <int WF, int MT, int RPW, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int S = a.S;
+    const GemvLayout L = gemv_layout(WF, MT, RPW, S, PRO, a.K, a.G);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = a.K, N = a.N, G = a.G, M = a.M;
+    const int R = L.R, ng = L.ng;
+    const int ntiles = (N + R - 1) / R;
+
+    int8_t* act = reinterpret_cast<int8_t*>(smem + L.off_act);
+    int* asum = reinterpret_cast<int*>(smem + L.off_asum);
+    float* as = reinterpret_cast<float*>(smem + L.off_as);
+    int* s_abort = reinterpret_cast<int*>(smem + L.off_as + align_up(MT * 4, 16));
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.off_bar);
+    int* gsbuf = reinterpret_cast<int*>(smem + L.off_gs) + warp * L.pairs * L.gpj;
+    uint16_t* outt = reinterpret_cast<uint16_t*>(smem + L.off_out);
+
+    const uint8_t* wbase = reinterpret_cast<const uint8_t*>(a.w);
+    auto issue = [&](int t, int s) {
+        uint8_t* st = smem + L.off_stage + s * L.stage_bytes;
+        const int rows = min(R, N - t * R);
+        const unsigned wb = (unsigned)(rows * L.wrow);
+        const unsigned sb_all = (unsigned)(rows * ng * 2);
+        const unsigned sb = sb_all & ~15u;
+        mbar_arrive_expect_tx(&bar[s], wb + sb);
+        tma_load_1d(st, wbase + (size_t)t * R * L.wrow, wb, &bar[s]);
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(a.ws) + (size_t)t * R * ng;
+        if (sb) tma_load_1d(st + L.stage_w, sc, sb, &bar[s]);
+        for (unsigned i = sb / 2; i < sb_all / 2; ++i)  // sub-16-byte remainder of a partial tile
+            reinterpret_cast<uint16_t*>(st + L.stage_w)[i] = sc[i];
+    };
+
+    if (tid == 0) {
+        *s_abort = 0;
+        for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0)
+        for (int s = 0; s < S; ++s) {
+            const int t = blockIdx.x + s * gridDim.x;
+            if (t < ntiles) issue(t, s);
+        }
+    // Weights are constant: their copies above may overlap the previous kernel.
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // ---------------------------------------------------------- prologue: activations -> smem int8
+    if constexpr (PRO == (int)Pro::PREQ) {
+        for (int i = tid; i < M * K; i += kGemvThreads) {
+            const int m = i / K, k = i % K;
+            int8_t v = a.aq[i];
+            if constexpr (WF == 1) {
+                const int blk = k >> 3, e = k & 7;
+                act[m * K + blk * 8 + ((e & 1) ? 4 + (e >> 1) : (e >> 1))] = v;
+            } else {
+                act[i] = v;
+            }
+        }
+        if (tid < M) as[tid] = a.as[tid];
+        __syncthreads();
+    } else {
+        __half* xs = reinterpret_cast<__half*>(smem + L.off_xs);
+        float* red = reinterpret_cast<float*>(smem + L.off_gs);  // scratch before the main loop
+        for (int m = 0; m < M; ++m) {
+            const __half* xm = a.x + (size_t)m * K;
+            float inv_rms = 0.0f;
+            __half inv16 = __float2half_rn(0.0f);
+            if constexpr (PRO == (int)Pro::RMSNORM_QUANT) {
+                for (int k = tid; k < K; k += kGemvThreads) xs[m * K + k] = xm[k];
+                __syncthreads();
+                if (warp == 0) {
+                    float ss = rms_sumsq_warp(xs + m * K, K);
+                    if (lane == 0) red[0] = ss;
+                }
+                __syncthreads();
+                const float ss = red[0];
+                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps));
+                inv_rms = __fdiv_rn(1.0f, rms);
+                inv16 = __float2half_rn(inv_rms);
+                __syncthreads();
+            }
+            const int vec_end = (K / 8) * 8;
+            // pass 1: (normalize and) absmax
+            float mx = 0.0f;
+            for (int k = tid; k < K; k += kGemvThreads) {
+                __half v = xm[k];
+                if constexpr (PRO == (int)Pro::RMSNORM_QUANT) {
+                    __half xv = xs[m * K + k];
+                    v = (k < vec_end) ? __hmul(__hmul(xv, inv16), a.norm_w[k])
+                                      : __float2half_rn(__fmul_rn(__fmul_rn(h2f(xv), inv_rms), h2f(a.norm_w[k])));
+                    xs[m * K + k] = v;
+                }
+                mx = fmaxf(mx, fabsf(h2f(v)));
+            }
+            mx = warp_max(mx);
+            if (lane == 0) red[warp] = mx;
+            __syncthreads();
+            if (warp == 0) {
+                float v = lane < kGemvWarps ? red[lane] : 0.0f;
+                v = warp_max(v);
+                if (lane == 0) red[16] = v;
+            }
+            __syncthreads();
+            float scale = __fdiv_rn(red[16], 127.0f);
+            if (scale < 1e-10f) scale = 1e-10f;
+            const float inv = __fdiv_rn(1.0f, scale);
+            if (tid == 0) as[m] = scale;
+            // pass 2: quantize
+            for (int k = tid; k < K; k += kGemvThreads) {
+                const __half v = (PRO == (int)Pro::RMSNORM_QUANT) ? xs[m * K + k] : xm[k];
+                const int8_t q = quant_act(h2f(v), inv, k < vec_end);
+                if constexpr (WF == 1) {
+                    const int blk = k >> 3, e = k & 7;
+                    act[m * K + blk * 8 + ((e & 1) ? 4 + (e >> 1) : (e >> 1))] = q;
+                } else {
+                    act[m * K + k] = q;
+                }
+                if (a.aq_out && blockIdx.x == 0) a.aq_out[(size_t)m * K + k] = q;
+            }
+            if (a.as_out && blockIdx.x == 0 && tid == 0) a.as_out[m] = scale;
+            __syncthreads();
+        }
+    }
+    if constexpr (WF == 1) {  // per-group activation sums for the unsigned-nibble dot product
+        for (int i = tid; i < M * ng; i += kGemvThreads) {
+            const int m = i / ng, g = i % ng;
+            int s = 0;
+            for (int k = 0; k < G; ++k) s += act[m * K + g * G + k];  // permutation stays inside 8-blocks
+            asum[i] = s;
+        }
+        __syncthreads();
+    }
+
+    // ---------------------------------------------------------- main loop over tiles
+    const int chunks = K / 16 / (WF == 1 ? 2 : 1);  // 16-byte weight chunks per row
+    const int npass = (chunks + 31) / 32;
+    const int lanes_per_group = WF == 0 ? G / 16 : G / 32;
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int s = it % S;
+        const unsigned par = (unsigned)((it / S) & 1);
+        if (!mbar_wait_bounded(&bar[s], par)) {
+            report_dev_error(kDevTmaTimeout);
+            atomicExch(s_abort, 1);
+        }
+        __syncthreads();
+        if (*s_abort) return;  // uniform across the block
+        const uint8_t* st = smem + L.off_stage + s * L.stage_bytes;
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + L.stage_w);
+        uint16_t* ob = outt + (it & 1) * R * MT;
+        const int rows_valid = min(R, N - t * R);
+
+        float run0 = 0.0f;
+        const int my_pair = lane;  // owner lane for pair (r, m) = lane
+        const int my_r = my_pair / MT, my_m = my_pair % MT;
+        for (int pass = 0; pass < npass; ++pass) {
+            const int c = pass * 32 + lane;
+            const bool cval = c < chunks;
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+                const int row = warp * RPW + r;
+                int4 wv = make_int4(0, 0, 0, 0);
+                if (cval && row < rows_valid) wv = *reinterpret_cast<const int4*>(st + row * L.wrow + c * 16);
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    int acc = 0;
+                    if (cval && m < M) {
+                        if constexpr (WF == 0) {
+                            const int4 av = *reinterpret_cast<const int4*>(act + m * K + c * 16);
+                            acc = dp4a_ss(av.x, wv.x, acc);
+                            acc = dp4a_ss(av.y, wv.y, acc);
+                            acc = dp4a_ss(av.z, wv.z, acc);
+                            acc = dp4a_ss(av.w, wv.w, acc);
+                        } else {
+                            const int4 a0 = *reinterpret_cast<const int4*>(act + m * K + c * 32);
+                            const int4 a1 = *reinterpret_cast<const int4*>(act + m * K + c * 32 + 16);
+                            const unsigned ww[4] = {(unsigned)wv.x, (unsigned)wv.y, (unsigned)wv.z, (unsigned)wv.w};
+                            const int ae[4] = {a0.x, a0.z, a1.x, a1.z};
+                            const int ao[4] = {a0.y, a0.w, a1.y, a1.w};
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const unsigned lo = (ww[q] & 0x0F0F0F0Fu) ^ 0x08080808u;
+                                const unsigned hi = ((ww[q] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+                                acc = dp4a_su(ae[q], lo, acc);
+                                acc = dp4a_su(ao[q], hi, acc);
+                            }
+                        }
+                    }
+                    for (int o = 1; o < lanes_per_group; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                    if ((lane % lanes_per_group) == 0 && cval) {
+                        const int g = (WF == 0 ? c * 16 : c * 32) / G;
+                        if constexpr (WF == 1) acc -= 8 * asum[m * ng + g];
+                        gsbuf[(r * MT + m) * L.gpj + (g - pass * L.gpj)] = acc;
+                    }
+                }
+            }
+            __syncwarp();
+            if (my_pair < L.pairs) {
+                const int row = warp * RPW + my_r;
+                const int g0 = pass * L.gpj;
+                const int g1 = min(ng, g0 + L.gpj);
+                const int* gs = gsbuf + my_pair * L.gpj;
+                for (int g = g0; g < g1; ++g)
+                    run0 = fmaf((float)gs[g - g0], h2f_bits(sc[row * ng + g]), run0);
+            }
+            __syncwarp();
+        }
+        if (my_pair < L.pairs) {
+            const int row = warp * RPW + my_r;
+            if (my_m < M) ob[row * MT + my_m] = f2h_bits(__fmul_rn(run0, as[my_m]));
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const int tn = t + S * (int)gridDim.x;
+            if (tn < ntiles) issue(tn, s);
+        }
+        // ------------------------------------------------------ epilogue from the smem tile
+        if constexpr (EPI == (int)Epi::STORE || EPI == (int)Epi::RESIDUAL) {
+            for (int i = tid; i < rows_valid * M; i += kGemvThreads) {
+                const int m = i / rows_valid, row = i % rows_valid;
+                const int n = t * R + row;
+                __half v = __ushort_as_half(ob[row * MT + m]);
+                if constexpr (EPI == (int)Epi::RESIDUAL) v = __hadd(a.resid[(size_t)m * N + n], v);
+                a.out[(size_t)m * N + n] = v;
+            }
+        } else {
+            const int half_rows = rows_valid / 2;
+            for (int i = tid; i < half_rows * M; i += kGemvThreads) {
+                const int m = i / half_rows, hr = i % half_rows;
+                const __half gate = __ushort_as_half(ob[(2 * hr) * MT + m]);
+                const __half up = __ushort_as_half(ob[(2 * hr + 1) * MT + m]);
+                const __half act_g = (EPI == (int)Epi::GLU_SILU) ? ref_silu(gate) : ref_gelu(gate);
+                a.out[(size_t)m * (N / 2) + (t * R) / 2 + hr] = __hmul(act_g, up);
+            }
+        }
+    }
+}
+
+}  // namespace cb

@@ -1,0 +1,358 @@
+// Elementwise, normalisation, RoPE, KV-quantisation, softmax, embedding and argmax
+// kernels (sm_100a). Each kernel states the reference function whose arithmetic it
+// reproduces; see common.cuh for the rounding conventions.
+#include "common.cuh"
+#include "gemv.cuh"
+#include "ops.h"
+
+namespace cb {
+
+__device__ unsigned g_dev_error = 0;
+
+// ------------------------------------------------------------------ activation quantization
+// graph_ops_nn.cpp:35-66: per row absmax -> scale = max(absmax/127, 1e-10) -> int8 (RNE).
+__global__ void quantize_act_kernel(const __half* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scales,
+                                    int K) {
+    const int m = blockIdx.x;
+    const __half* xm = x + (size_t)m * K;
+    __shared__ float red[33];
+    float mx = 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(h2f(xm[k])));
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        v = warp_max(v);
+        if (threadIdx.x == 0) red[32] = v;
+    }
+    __syncthreads();
+    float scale = __fdiv_rn(red[32], 127.0f);
+    if (scale < 1e-10f) scale = 1e-10f;
+    const float inv = __fdiv_rn(1.0f, scale);
+    const int vec_end = (K / 8) * 8;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) q[(size_t)m * K + k] = quant_act(h2f(xm[k]), inv, k < vec_end);
+    if (threadIdx.x == 0) scales[m] = scale;
+}
+
+// ------------------------------------------------------------------ RMSNorm (kernel_attention.cpp:484-563)
+__global__ void rms_norm_kernel(const __half* __restrict__ x, const __half* __restrict__ w, __half* __restrict__ y,
+                                int dims, float eps) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __half* xs = reinterpret_cast<__half*>(sm);
+    __shared__ float ssum;
+    const size_t r = blockIdx.x;
+    for (int k = threadIdx.x; k < dims; k += blockDim.x) xs[k] = x[r * dims + k];
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float ss = rms_sumsq_warp(xs, dims);
+        if (threadIdx.x == 0) ssum = ss;
+    }
+    __syncthreads();
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, (float)dims), eps));
+    const float inv = __fdiv_rn(1.0f, rms);
+    const __half inv16 = __float2half_rn(inv);
+    const int vec_end = dims >= 8 ? (dims / 8) * 8 : 0;
+    for (int k = threadIdx.x; k < dims; k += blockDim.x) {
+        __half v = xs[k];
+        y[r * dims + k] = (k < vec_end) ? __hmul(__hmul(v, inv16), w[k])
+                                        : __float2half_rn(__fmul_rn(__fmul_rn(h2f(v), inv), h2f(w[k])));
+    }
+}
+
+// ------------------------------------------------------------------ RoPE (kernel_attention.cpp:614-676)
+// One thread per (token, head, i < D/2) rotation pair; cos/sin come from the fp16 tables
+// that the host builds with the reference's formula (cactus_rope_tables()).
+__global__ void rope_kernel(const __half* __restrict__ in, __half* __restrict__ out, const __half* __restrict__ ct,
+                            const __half* __restrict__ st, long long total_pairs, int seq_len, int num_heads,
+                            int head_dim, long long start_pos) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= total_pairs) return;
+    const int half = head_dim / 2;
+    const int i = (int)(idx % half);
+    const long long row = idx / half;  // (b*S + s)*H + h
+    const int s = (int)((row / num_heads) % seq_len);
+    const long long pos = start_pos + s;
+    const __half* xr = in + row * head_dim;
+    __half* yr = out + row * head_dim;
+    const __half c = ct[pos * half + i], sn = st[pos * half + i];
+    const __half x1 = xr[i], x2 = xr[i + half];
+    const int vec_half = (half / 8) * 8;
+    if (i < vec_half) {
+        yr[i] = __hfma(__hneg(x2), sn, __hmul(x1, c));
+        yr[i + half] = __hfma(x1, sn, __hmul(x2, c));
+    } else {
+        const float f1 = h2f(x1), f2 = h2f(x2), fc = h2f(c), fs = h2f(sn);
+        yr[i] = f2h(__fsub_rn(__fmul_rn(f1, fc), __fmul_rn(f2, fs)));
+        yr[i + half] = f2h(__fadd_rn(__fmul_rn(f2, fc), __fmul_rn(f1, fs)));
+    }
+}
+
+// ------------------------------------------------------------------ KV quantisation (kernel_quants.cpp:223-293)
+// One warp per (token*head, group): absmax -> scale -> RNE quantisation of the vector part.
+__global__ void quantize_kv_kernel(const __half* __restrict__ src, int8_t* __restrict__ dst, float* __restrict__ scales,
+                                   long long rows, int head_dim, int G) {
+    const int ng = (head_dim + G - 1) / G;
+    const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (wid >= rows * ng) return;
+    const long long row = wid / ng;
+    const int g = (int)(wid % ng);
+    const int g0 = g * G;
+    const int cnt = min(G, head_dim - g0);
+    const __half* hs = src + row * head_dim + g0;
+    float mx = 0.0f;
+    for (int k = lane; k < cnt; k += 32) mx = fmaxf(mx, fabsf(h2f(hs[k])));
+    mx = warp_max(mx);
+    float scale = __fdiv_rn(mx, 127.0f);
+    if (scale < 1e-10f) scale = 1e-10f;
+    const float inv = __fdiv_rn(1.0f, scale);
+    const int vec = (cnt / 8) * 8;
+    for (int k = lane; k < cnt; k += 32) {
+        const float v = __fmul_rn(h2f(hs[k]), inv);
+        dst[row * head_dim + g0 + k] = (int8_t)sat8(k < vec ? cvt_rne_sat(v) : (int)roundf(v));
+    }
+    if (lane == 0) scales[row * ng + g] = scale;
+}
+
+// ------------------------------------------------------------------ elementwise
+// Vector-path semantics for the first (n/8)*8 elements, scalar-tail semantics after.
+__global__ void silu_kernel(const __half* __restrict__ x, __half* __restrict__ y, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    if (i < (n / 8) * 8) {
+        y[i] = ref_silu(x[i]);
+    } else {
+        const float v = h2f(x[i]);
+        y[i] = f2h(__fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)))));
+    }
+}
+__global__ void gelu_kernel(const __half* __restrict__ x, __half* __restrict__ y, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    if (i < (n / 8) * 8) {
+        y[i] = ref_gelu(x[i]);
+    } else {
+        const float v = h2f(x[i]);
+        const float inner = __fmul_rn(0.7978845608028654f, fmaf(__fmul_rn(__fmul_rn(0.044715f, v), v), v, v));
+        y[i] = f2h(__fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner))));
+    }
+}
+// op: 0 add, 1 add clipped (fp32 add, clamp +-65500), 2 multiply
+__global__ void binary_kernel(const __half* __restrict__ a, const __half* __restrict__ b, __half* __restrict__ y,
+                              long long n, int op) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    if (op == 0) {
+        y[i] = __hadd(a[i], b[i]);
+    } else if (op == 1) {
+        float r = __fadd_rn(h2f(a[i]), h2f(b[i]));
+        r = fminf(fmaxf(r, -65500.0f), 65500.0f);
+        y[i] = f2h(r);
+    } else {
+        y[i] = __hmul(a[i], b[i]);
+    }
+}
+__global__ void scalar_mul_kernel(const __half* __restrict__ x, __half* __restrict__ y, long long n, __half s) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __hmul(x[i], s);
+}
+
+// ------------------------------------------------------------------ softmax (kernel_nn.cpp:152-251)
+// One warp per row. Lane e owns the reference's accumulator for offset e of every 32-wide
+// chunk, so the fp32 sum follows the NEON lane order exactly.
+__global__ void softmax_kernel(const __half* __restrict__ x, __half* __restrict__ y, int rows, int V) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const __half* in = x + (size_t)row * V;
+    __half* out = y + (size_t)row * V;
+    float mx = -INFINITY;
+    for (int i = lane; i < V; i += 32) mx = fmaxf(mx, h2f(in[i]));
+    mx = warp_max(mx);
+    const int vv = (V / 32) * 32;
+    float acc = 0.0f;
+    for (int i = lane; i < vv; i += 32) {
+        const float e = ref_fast_exp(__fsub_rn(h2f(in[i]), mx));
+        out[i] = f2h(e);
+        acc = __fadd_rn(acc, e);
+    }
+    // lane l (0..3): acc[l] + acc[4+l] + ... + acc[28+l], sequentially
+    float s = __shfl_sync(0xffffffffu, acc, lane & 3);
+    for (int u = 1; u < 8; ++u) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc, 4 * u + (lane & 3)));
+    const float l0 = __shfl_sync(0xffffffffu, s, 0), l1 = __shfl_sync(0xffffffffu, s, 1);
+    const float l2 = __shfl_sync(0xffffffffu, s, 2), l3 = __shfl_sync(0xffffffffu, s, 3);
+    float sum = __fadd_rn(__fadd_rn(l0, l1), __fadd_rn(l2, l3));
+    for (int i = vv; i < V; ++i) {  // scalar tail, in order (identical on all lanes)
+        const float e = expf(__fsub_rn(h2f(in[i]), mx));
+        if (lane == 0) out[i] = f2h(e);
+        sum = __fadd_rn(sum, e);
+    }
+    __syncwarp();
+    const float inv = __fdiv_rn(1.0f, sum);
+    const __half inv16 = __float2half_rn(inv);
+    for (int i = lane; i < vv; i += 32) out[i] = __hmul(out[i], inv16);
+    for (int i = vv + lane; i < V; i += 32) out[i] = f2h(__fmul_rn(h2f(out[i]), inv));
+}
+
+// ------------------------------------------------------------------ embedding (graph_ops_tensor.cpp:226-331)
+__global__ void embedding_int8_kernel(const int8_t* __restrict__ table, const __half* __restrict__ scales, int G,
+                                      int ng, int hidden, const uint32_t* __restrict__ ids, int n_ids,
+                                      __half* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)n_ids * hidden) return;
+    const int t = (int)(i / hidden), k = (int)(i % hidden);
+    const size_t row = ids[t];
+    out[i] = f2h(__fmul_rn((float)table[row * hidden + k], h2f(scales[row * ng + k / G])));
+}
+__global__ void embedding_f16_kernel(const __half* __restrict__ table, int hidden, const uint32_t* __restrict__ ids,
+                                     int n_ids, __half* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)n_ids * hidden) return;
+    const int t = (int)(i / hidden), k = (int)(i % hidden);
+    out[i] = table[(size_t)ids[t] * hidden + k];
+}
+
+// ------------------------------------------------------------------ argmax (kernel_nn.cpp:451-467)
+// Keys order by (value, then lower index): the first maximum wins as with the strict '>'.
+__device__ __forceinline__ unsigned long long argmax_key(float v, unsigned idx) {
+    if (v != v) return 0ull;  // NaN never compares greater
+    unsigned u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (0xFFFFFFFFu - idx);
+}
+__global__ void argmax_kernel(const __half* __restrict__ logits, int V, uint32_t* __restrict__ out) {
+    __shared__ unsigned long long red[32];
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const unsigned long long k = argmax_key(h2f(logits[i]), (unsigned)i);
+        best = k > best ? k : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+            best = k > best ? k : best;
+        }
+        if (threadIdx.x == 0) out[0] = best == 0ull ? 0u : 0xFFFFFFFFu - (unsigned)(best & 0xFFFFFFFFull);
+    }
+}
+
+// ------------------------------------------------------------------ INT4 unpack (kernel_quants.cpp:295-351)
+__global__ void unpack_int4_kernel(const uint8_t* __restrict__ p, int8_t* __restrict__ o, long long count) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    const uint8_t b = p[i >> 1];
+    int v = (i & 1) ? (b >> 4) : (b & 0x0F);
+    o[i] = (int8_t)((v & 8) ? v - 16 : v);
+}
+
+// ------------------------------------------------------------------ FP16 matmul (kernel_gemm.cpp:17-126)
+// fp16 accumulation in the reference's 8 lanes: thread j of an 8-thread group owns lane j of
+// one output and performs the same sequence of fp16 FMAs; the lanes are folded with the
+// reference's fp16 horizontal-sum tree (kernel_gemm.cpp:8-15).
+__global__ void matmul_f16_kernel(const __half* __restrict__ A, const __half* __restrict__ Bt, __half* __restrict__ C,
+                                  int M, int K, int N) {
+    const int j = threadIdx.x & 7;
+    const long long n = (long long)blockIdx.x * (blockDim.x >> 3) + (threadIdx.x >> 3);
+    const bool valid = n < N;
+    const int K16 = (K / 16) * 16, K8 = (K / 8) * 8;
+    const __half* b = Bt + (valid ? n : 0) * (long long)K;
+    for (int m = 0; m < M; ++m) {
+        const __half* a = A + (size_t)m * K;
+        __half acc = __float2half_rn(0.0f);
+        if (valid) {
+            for (int k = 0; k < K16; k += 16) {
+                acc = __hfma(a[k + j], b[k + j], acc);
+                acc = __hfma(a[k + 8 + j], b[k + 8 + j], acc);
+            }
+            for (int k = K16; k < K8; k += 8) acc = __hfma(a[k + j], b[k + j], acc);
+            if (j == 0)
+                for (int k = K8; k < K; ++k) acc = f2h(fmaf(h2f(a[k]), h2f(b[k]), h2f(acc)));
+        }
+        // hsum: lo+hi, then (0+2),(1+3), then (0)+(1)
+        __half t = __hadd(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
+        __half u = __hadd(t, __shfl_down_sync(0xffffffffu, t, 2, 8));
+        __half v = __hadd(u, __shfl_down_sync(0xffffffffu, u, 1, 8));
+        if (valid && j == 0) C[(size_t)m * N + n] = v;
+    }
+}
+
+}  // namespace cb
+
+// ==================================================================== host launchers
+namespace cb {
+
+static inline unsigned nblocks(long long n, int t) { return (unsigned)((n + t - 1) / t); }
+
+int launch_quantize_act(const __half* x, int8_t* q, float* s, int M, int K, cudaStream_t st) {
+    quantize_act_kernel<<<M, 256, 0, st>>>(x, q, s, K);
+    return 0;
+}
+int launch_rms_norm(const __half* x, const __half* w, __half* y, int rows, int dims, float eps, cudaStream_t st) {
+    const size_t sm = (size_t)dims * 2;
+    if (sm > 48 * 1024) cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    rms_norm_kernel<<<rows, 256, sm, st>>>(x, w, y, dims, eps);
+    return 0;
+}
+int launch_rope(const __half* in, __half* out, const __half* ct, const __half* stab, long long rows, int seq_len,
+                int heads, int head_dim, long long start_pos, cudaStream_t st) {
+    const long long pairs = rows * (head_dim / 2);
+    rope_kernel<<<nblocks(pairs, 256), 256, 0, st>>>(in, out, ct, stab, pairs, seq_len, heads, head_dim, start_pos);
+    return 0;
+}
+int launch_quantize_kv(const __half* src, int8_t* dst, float* scales, long long rows, int head_dim, int G,
+                       cudaStream_t st) {
+    const int ng = (head_dim + G - 1) / G;
+    quantize_kv_kernel<<<nblocks(rows * ng * 32, 256), 256, 0, st>>>(src, dst, scales, rows, head_dim, G);
+    return 0;
+}
+int launch_silu(const __half* x, __half* y, long long n, cudaStream_t st) {
+    silu_kernel<<<nblocks(n, 256), 256, 0, st>>>(x, y, n);
+    return 0;
+}
+int launch_gelu(const __half* x, __half* y, long long n, cudaStream_t st) {
+    gelu_kernel<<<nblocks(n, 256), 256, 0, st>>>(x, y, n);
+    return 0;
+}
+int launch_binary(const __half* a, const __half* b, __half* y, long long n, int op, cudaStream_t st) {
+    binary_kernel<<<nblocks(n, 256), 256, 0, st>>>(a, b, y, n, op);
+    return 0;
+}
+int launch_scalar_mul(const __half* x, __half* y, long long n, float s, cudaStream_t st) {
+    scalar_mul_kernel<<<nblocks(n, 256), 256, 0, st>>>(x, y, n, __float2half_rn(s));
+    return 0;
+}
+int launch_softmax(const __half* x, __half* y, int rows, int V, cudaStream_t st) {
+    softmax_kernel<<<nblocks((long long)rows * 32, 128), 128, 0, st>>>(x, y, rows, V);
+    return 0;
+}
+int launch_embedding_int8(const int8_t* t, const __half* s, int G, int hidden, const uint32_t* ids, int n,
+                          __half* out, cudaStream_t st) {
+    embedding_int8_kernel<<<nblocks((long long)n * hidden, 256), 256, 0, st>>>(t, s, G, hidden / G, hidden, ids, n, out);
+    return 0;
+}
+int launch_embedding_f16(const __half* t, int hidden, const uint32_t* ids, int n, __half* out, cudaStream_t st) {
+    embedding_f16_kernel<<<nblocks((long long)n * hidden, 256), 256, 0, st>>>(t, hidden, ids, n, out);
+    return 0;
+}
+int launch_argmax(const __half* logits, int V, uint32_t* out, cudaStream_t st) {
+    argmax_kernel<<<1, 1024, 0, st>>>(logits, V, out);
+    return 0;
+}
+int launch_unpack_int4(const uint8_t* p, int8_t* o, long long count, cudaStream_t st) {
+    unpack_int4_kernel<<<nblocks(count, 256), 256, 0, st>>>(p, o, count);
+    return 0;
+}
+int launch_matmul_f16(const __half* A, const __half* Bt, __half* C, int M, int K, int N, cudaStream_t st) {
+    matmul_f16_kernel<<<nblocks((long long)N * 8, 256), 256, 0, st>>>(A, Bt, C, M, K, N);
+    return 0;
+}
+
+}  // namespace cb

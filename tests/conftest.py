@@ -35,3 +35,13 @@ def ref():
     from oracle import refcpu
     refcpu.lib()
     return refcpu
+
+
+@pytest.fixture(autouse=True)
+def _release_device_temporaries():
+    yield
+    if "tests.gpu_util" in sys.modules:
+        try:
+            sys.modules["tests.gpu_util"].release()
+        except Exception:
+            pass
