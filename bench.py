@@ -1,0 +1,358 @@
+#!/usr/bin/env python3
+"""Benchmark of the Cactus hot path on B200.
+
+Workload (one "step" = one request): Qwen3-0.6B-shaped decoder, random-init INT8 weights
+(group 32, N(0,0.02), numpy default_rng(0)), batch 1, a 128-token random prompt
+(prefill of 127 tokens) followed by 128 greedy decode steps, run through the engine's
+C ABI (cactus_engine_generate_greedy) with host prompt / token buffers.
+
+  value : decode tokens/s over all ranks, decode-phase device time (CUDA events on the
+          engine stream; the prompt is already consumed, weights resident in HBM)
+  e2e   : generated tokens/s over the whole C-ABI call (prompt H2D, prefill, 128 decode
+          steps, tokens D2H), host wall clock around the call
+Weights (596 MB INT8 + 37 MB scales) exceed the 126 MB L2, so no L2 flush is needed.
+
+N > 1 GPUs (torchrun): every rank serves its own independent request stream on its own
+GPU (replicas, no collective on the data path); value = all ranks' tokens / max rank time.
+
+`--impl reference` times the CPU restatement of the reference kernels (oracle/, the
+reference's NEON code does not build on x86) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT = 128
+DECODE = 128
+GROUP = 32
+METRIC = "qwen3-0.6b int8 batch-1 decode tok/s per job (1-8 B200 replicas)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline sample")
+    ap.add_argument("--no-kernel-timing", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def model_folder():
+    from cactus_b200 import convert
+    arch = convert.qwen3_0_6b(GROUP)
+    os.environ.setdefault("CACTUS_B200_MODELS", "/tmp/cactus_b200_models")
+    return arch, convert.default_model_dir(arch, seed=0)
+
+
+def ensure_model(rank, world, barrier):
+    from cactus_b200 import convert
+    arch, folder = model_folder()
+    if rank == 0:
+        convert.make_model(folder, arch, seed=0)
+    barrier()
+    return arch, folder
+
+
+def bytes_per_token(arch, ctx):
+    """Algorithmic HBM bytes of one batch-1 decode token: weights + scales once, the KV cache
+    of `ctx` cached tokens once (INT8 + fp32 scales per 128-group), activations negligible."""
+    H, F, D, Hq, Hkv = arch.hidden_dim, arch.ffn_intermediate_dim, arch.attention_head_dim, arch.attention_heads, \
+        arch.attention_kv_heads
+    per_layer = (Hq + 2 * Hkv) * D * H + H * Hq * D + 2 * F * H + H * F
+    w = arch.num_layers * per_layer + arch.vocab_size * H
+    scales = w // GROUP * 2
+    kv = arch.num_layers * ctx * Hkv * (2 * D + 2 * 4 * ((D + 127) // 128))
+    return w + scales + kv
+
+
+class ClockSampler:
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        mhz = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) >= 9:
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": float(np.median(mhz)) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def gemv_kernel_timing(arch, dev_index):
+    """Times the grouped INT8 GEMV (the dominant kernel: every projection of a decode token)
+    with CUDA events around a CUDA graph of one token's 4*28+1 GEMV launches over distinct
+    weights (596 MB > L2), launched through the C ABI on torch's stream."""
+    import torch
+    import cactus_b200 as cb
+    L = cb.lib()
+    H, F, D, Hq, Hkv = arch.hidden_dim, arch.ffn_intermediate_dim, arch.attention_head_dim, arch.attention_heads, \
+        arch.attention_kv_heads
+    shapes = []
+    for _ in range(arch.num_layers):
+        shapes += [((Hq + 2 * Hkv) * D, H), (H, Hq * D), (2 * F, H), (H, F)]
+    shapes.append((arch.vocab_size, H))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    bufs = []
+    total_bytes = 0
+    for N, K in shapes:
+        w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g)
+        s = (torch.rand((N, K // GROUP), device="cuda", generator=g) * 1e-3).half()
+        x = torch.randn((1, K), device="cuda", generator=g).half()
+        y = torch.empty((1, N), device="cuda", dtype=torch.half)
+        bufs.append((w, s, x, y, N, K))
+        total_bytes += N * K + N * (K // GROUP) * 2 + K * 2 + N * 2
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        sp = stream.cuda_stream
+
+        def launch():
+            for w, s, x, y, N, K in bufs:
+                rc = L.cactus_cuda_linear_int8(x.data_ptr(), w.data_ptr(), s.data_ptr(), y.data_ptr(), 1, K, N, GROUP,
+                                               sp)
+                if rc:
+                    raise RuntimeError(L.cactus_cuda_last_error().decode())
+        for _ in range(3):
+            launch()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            launch()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+    del graph
+    return {"launches": len(shapes), "bytes": total_bytes, "ms": ms}
+
+
+def cpu_baseline_sample(folder, prompt, n_tokens=4):
+    """Decode tok/s of the CPU restatement (all host threads), bounded sample."""
+    from oracle import model as OM
+    from oracle import refcpu
+    refcpu.set_threads(os.cpu_count() or 1)
+    m = OM.RefModel(folder, context_size=512)
+    m.kv.reset()
+    m.prefill(prompt[:-1])
+    tok = prompt[-1]
+    t0 = time.perf_counter()
+    for _ in range(n_tokens):
+        tok = m.decode_argmax([tok])
+    dt = time.perf_counter() - t0
+    return {"value": n_tokens / dt, "unit": "tok/s", "cores": refcpu.threads(), "kind": "port",
+            "sample": f"{n_tokens} greedy decode tokens after a {len(prompt) - 1}-token prefill, Qwen3-0.6B INT8 "
+                      f"G{GROUP}, oracle/refcpu (C, OpenMP) restatement of the reference kernels; the NEON "
+                      "reference does not build on x86"}
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return 0
+    arch, folder = model_folder()
+    from cactus_b200 import convert
+    convert.make_model(folder, arch, seed=0)
+    from oracle import model as OM
+    from oracle import refcpu
+    refcpu.set_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, arch.vocab_size, PROMPT).tolist()
+    m = OM.RefModel(folder, context_size=512)
+    m.prefill(prompt[:-1])
+    tok = prompt[-1]
+    per_step = 2
+    for _ in range(args.warmup):
+        for _ in range(per_step):
+            tok = m.decode_argmax([tok])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for _ in range(per_step):
+            tok = m.decode_argmax([tok])
+    dt = time.perf_counter() - t0
+    v = args.steps * per_step / dt
+    sample = (f"{per_step} greedy decode tokens per step after a {PROMPT - 1}-token prefill (Qwen3-0.6B INT8 G{GROUP}); "
+              "oracle/refcpu C restatement, OpenMP over all host threads (NEON reference does not build on x86)")
+    line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic (random-init weights, random ids)",
+            "impl": "reference",
+            "config": {"workload": f"qwen3-0.6b int8 g{GROUP} batch1 prompt{PROMPT} decode", "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": refcpu.threads(), "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+        pg = dist
+
+    def barrier():
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    arch, folder = ensure_model(rank, world, barrier)
+    from cactus_b200.engine import Engine
+    eng = Engine(folder, context_size=512, max_batch=1, device=local_rank)
+    rng = np.random.default_rng(1000 + rank)
+    prompts = [rng.integers(0, arch.vocab_size, PROMPT).astype(np.uint32) for _ in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        eng.generate_greedy(prompts[i], DECODE)
+    barrier()
+    dec_ms = pre_ms = wall = 0.0
+    launches = 0
+    graph_replays = 0
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        for i in range(args.steps):
+            t0 = time.perf_counter()
+            toks = eng.generate_greedy(prompts[args.warmup + i], DECODE)
+            wall += time.perf_counter() - t0
+            st = eng.stats()
+            dec_ms += st["decode_ms"]
+            pre_ms += st["prefill_ms"]
+            launches += int(st["launches"])
+            graph_replays += int(st["graph_replays"])
+        barrier()
+    assert toks.shape == (DECODE,)
+    vals = torch.tensor([dec_ms, pre_ms, wall * 1e3, float(launches)], dtype=torch.float64, device="cuda")
+    if pg:
+        mx = vals.clone()
+        pg.all_reduce(mx, op=pg.ReduceOp.MAX)
+        sm = vals.clone()
+        pg.all_reduce(sm, op=pg.ReduceOp.SUM)
+        dec_max, pre_max, wall_max, launches_all = mx[0].item(), mx[1].item(), mx[2].item(), sm[3].item()
+    else:
+        dec_max, pre_max, wall_max, launches_all = dec_ms, pre_ms, wall * 1e3, float(launches)
+    kern = None
+    if rank == 0 and not args.no_kernel_timing:
+        eng_bytes = eng.stats()["weight_bytes"]
+        kern = gemv_kernel_timing(arch, local_rank)
+        del eng_bytes
+    out = None
+    if rank == 0:
+        ntok = world * args.steps * DECODE
+        value = ntok / (dec_max / 1e3)
+        e2e = ntok / (wall_max / 1e3)
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+            os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+        hbm = float(peaks.get("hbm_gbs", 6650.0))
+        peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+        avg_ctx = PROMPT + DECODE / 2
+        bpt = bytes_per_token(arch, avg_ctx)
+        per_tok_s = dec_max / 1e3 / (args.steps * DECODE)
+        roof = None
+        if kern:
+            achieved = kern["bytes"] / (kern["ms"] / 1e3) / 1e9
+            traffic = None
+            tf = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+            if os.path.exists(tf):
+                traffic = json.load(open(tf)).get("traffic_bytes_per_launch")
+            roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                    "traffic": traffic, "peak_source": peak_src,
+                    "kernel": "qgemv_kernel (grouped INT8 GEMV, M=1)",
+                    "algorithmic_bytes_per_launch": kern["bytes"] / kern["launches"],
+                    "avg_launch_us": kern["ms"] * 1e3 / kern["launches"]}
+        out = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": (dec_max + pre_max) / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (random-init N(0,0.02) weights, random prompt ids)",
+            "config": {"workload": f"qwen3-0.6b int8 g{GROUP} batch1 prompt{PROMPT} decode{DECODE}",
+                       "model": "qwen3-0.6b-shaped (28L, hidden 1024, 16/8 heads, ffn 3072, vocab 151936)",
+                       "global_batch": world, "seq_len": PROMPT + DECODE, "parallelism": f"replicas x{world}",
+                       "l2": "weights 633 MB > 126 MB L2 (no flush needed)"},
+            "prefill_tok_s": world * args.steps * (PROMPT - 1) / (pre_max / 1e3),
+            "token_roofline": {"bytes_per_token": bpt, "achieved_gbs": bpt / per_tok_s / 1e9,
+                               "frac": bpt / per_tok_s / 1e9 / hbm, "peak": hbm, "avg_context": avg_ctx},
+            "roofline": roof,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
+                    "d2h_bytes_per_step": DECODE * 4},
+            "gpu_launches": int(launches_all),
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.skip_cpu:
+            try:
+                out["cpu_baseline"] = cpu_baseline_sample(folder, prompts[0].tolist())
+            except Exception as e:  # report, do not hide
+                out["cpu_baseline"] = {"error": str(e)}
+    eng.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    if out:
+        print(json.dumps(out), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

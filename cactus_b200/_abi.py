@@ -23,6 +23,7 @@ _SCALAR = {
     "bool": C.c_bool,
     "void": None,
     "cactus_model_t": C.c_void_p,
+    "cactus_engine_t": C.c_void_p,
     "cactus_token_callback": C.c_void_p,
 }
 

@@ -250,11 +250,22 @@ CB_API int cactus_cuda_attention_hybrid_int8_fp16(const uint16_t* queries, const
         (reinterpret_cast<uintptr_t>(values_cached) & 7))
         return fail(CB_ERR_ARG, "attention_hybrid: misaligned K/V");
     if (scale == 0.0f) scale = 1.0f / sqrtf((float)head_dim);
-    cb::launch_attention_hybrid(H(queries), keys_cached, values_cached, k_scales, v_scales, H(keys_new),
-                                H(values_new), H(output), (int)batch_size, (int)seq_len, (int)cache_len, (int)new_len,
-                                (int)num_q_heads, (int)num_kv_heads, (int)head_dim, scale, (long long)position_offset,
-                                is_causal, (int)quant_group_size, (long long)(cache_len * num_kv_heads * head_dim), 0,
-                                S(stream));
+    // The reference-order kernel (bit-exact) is used unless a long context would leave most
+    // SMs idle; then the keys are split across warps (same math, different fp32 rounding).
+    const size_t items = batch_size * num_q_heads * seq_len;
+    const bool exact = (cache_len + new_len) <= 4096 || items >= 2 * cb::kNumSMs;
+    const long long kc_bs = (long long)(cache_len * num_kv_heads * head_dim);
+    if (!exact || cb::launch_attention_hybrid_exact(H(queries), keys_cached, values_cached, k_scales, v_scales,
+                                                     H(keys_new), H(values_new), H(output), (int)batch_size,
+                                                     (int)seq_len, (int)cache_len, (int)new_len, (int)num_q_heads,
+                                                     (int)num_kv_heads, (int)head_dim, scale,
+                                                     (long long)position_offset, is_causal, (int)quant_group_size,
+                                                     kc_bs, 0, S(stream)) != 0)
+        cb::launch_attention_hybrid(H(queries), keys_cached, values_cached, k_scales, v_scales, H(keys_new),
+                                    H(values_new), H(output), (int)batch_size, (int)seq_len, (int)cache_len,
+                                    (int)new_len, (int)num_q_heads, (int)num_kv_heads, (int)head_dim, scale,
+                                    (long long)position_offset, is_causal, (int)quant_group_size, kc_bs, 0,
+                                    S(stream));
     return check_launch("attention_hybrid_int8_fp16");
 }
 

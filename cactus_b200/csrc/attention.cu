@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(128) attn_f16_kernel(const __half* __restrict_
         }
         const float bmax = warp_max(s);
         if (bmax > -INFINITY) {
-            const float corr = expf(__fsub_rn(run_max, bmax));
+            const float corr = expf_cr(__fsub_rn(run_max, bmax));
             run_sum = __fmul_rn(run_sum, corr);
             for (int i = 0; i < dpl; ++i) acc[i] = __fmul_rn(acc[i], corr);
             run_max = bmax;
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(128) attn_f16_kernel(const __half* __restrict_
         const int vec = (bs / 4) * 4;
         float y = 0.0f;
         if (lane < vec) y = (s == -INFINITY) ? 0.0f : attn_quad_exp(s, bmax);
-        else if (lane < bs) y = (s == -INFINITY) ? 0.0f : expf(__fsub_rn(s, bmax));
+        else if (lane < bs) y = (s == -INFINITY) ? 0.0f : expf_cr(__fsub_rn(s, bmax));
         // block sum in the reference order: quads ((y0+y1)+(y2+y3)) in sequence, then the tail
         const float y1 = __shfl_down_sync(0xffffffffu, y, 1), y2 = __shfl_down_sync(0xffffffffu, y, 2),
                     y3 = __shfl_down_sync(0xffffffffu, y, 3);
@@ -119,7 +119,12 @@ __global__ void __launch_bounds__(128) attn_hybrid_kernel(
     const __half* __restrict__ Q, const int8_t* __restrict__ Kc, const int8_t* __restrict__ Vc,
     const float* __restrict__ ks, const float* __restrict__ vs, const __half* __restrict__ Kn,
     const __half* __restrict__ Vn, __half* __restrict__ O, int B, int S, int cache_len, int new_len, int Hq, int Hkv,
-    int D, float scale, long long pos_off, int causal, int qgs, long long kc_bstride, long long sc_bstride) {
+    int D, float scale, long long pos_off, int causal, int qgs, long long kc_bstride, long long sc_bstride,
+    const int* __restrict__ dstate) {
+    if (dstate) {  // engine decode graphs keep {cache_len, total_len} in device memory
+        cache_len = dstate[0];
+        pos_off = dstate[1];
+    }
     __shared__ float qs[kMaxHeadDim];
     __shared__ float wmax[4], wsum[4];
     __shared__ float wacc[4][kMaxHeadDim];
@@ -177,12 +182,12 @@ __global__ void __launch_bounds__(128) attn_hybrid_kernel(
         }
         const float bmax = warp_max(s);
         if (bmax > -INFINITY) {
-            const float corr = expf(__fsub_rn(run_max, bmax));
+            const float corr = expf_cr(__fsub_rn(run_max, bmax));
             run_sum = __fmul_rn(run_sum, corr);
             for (int i = 0; i < dpl; ++i) acc[i] = __fmul_rn(acc[i], corr);
             run_max = bmax;
         }
-        const float y = (lane < bs && s != -INFINITY) ? expf(__fsub_rn(s, bmax)) : 0.0f;
+        const float y = (lane < bs && s != -INFINITY) ? expf_cr(__fsub_rn(s, bmax)) : 0.0f;
         float bsum = 0.0f;
         for (int i = 0; i < bs; ++i) {
             const float w = __shfl_sync(0xffffffffu, y, i);
@@ -212,7 +217,7 @@ __global__ void __launch_bounds__(128) attn_hybrid_kernel(
         float tot = 0.0f;
         float f[4];
         for (int w = 0; w < 4; ++w) {
-            f[w] = (wmax[w] == -INFINITY) ? 0.0f : expf(__fsub_rn(wmax[w], m));
+            f[w] = (wmax[w] == -INFINITY) ? 0.0f : expf_cr(__fsub_rn(wmax[w], m));
             tot = fmaf(wsum[w], f[w], tot);
         }
         __half* o = O + (((size_t)b * S + qp) * Hq + h) * D;
@@ -230,6 +235,213 @@ __global__ void __launch_bounds__(128) attn_hybrid_kernel(
     }
 }
 
+
+// ------------------------------------------------------------------ exact hybrid attention
+// Bit-for-bit restatement of cactus_attention_hybrid_int8_fp16's arithmetic: one CTA of 256
+// threads per (batch, q head, query) walks the 32-key blocks in order with the same online
+// softmax (corrections, block sums, fused V accumulation per dim) as the reference.
+// Thread (i = t/8, j = t%8) forms lane j of key i's 8-lane dot product; threads t < D own
+// output dim t. Raw INT8 K/V of the next blocks stream into shared memory with cp.async
+// (three buffers) while the current block is computed.
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int D>
+__global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
+    const __half* __restrict__ Q, const int8_t* __restrict__ Kc, const int8_t* __restrict__ Vc,
+    const float* __restrict__ ks, const float* __restrict__ vs, const __half* __restrict__ Kn,
+    const __half* __restrict__ Vn, __half* __restrict__ O, int S, int cache_len, int new_len, int Hq, int Hkv,
+    float scale, long long pos_off, int causal, int qgs, long long kc_bstride, long long sc_bstride,
+    const int* __restrict__ dstate) {
+    if (dstate) {
+        cache_len = dstate[0];
+        pos_off = dstate[1];
+    }
+    constexpr int KS = D + 8;       // padded float stride of the key tile
+    constexpr int RAW = 32 * D;     // bytes of one block of INT8 keys (or values)
+    constexpr int NBUF = 3;
+    extern __shared__ __align__(16) uint8_t smem[];
+    float* kf = reinterpret_cast<float*>(smem);  // [32][KS]
+    float* vf = kf + 32 * KS;                    // [32][D]
+    float* qs = vf + 32 * D;                     // [D]
+    float* sc = qs + D;                          // [32]
+    float* rsc = sc + 32;                        // raw scales [NBUF][2][32][nqg<=2]
+    int8_t* raw = reinterpret_cast<int8_t*>(rsc + NBUF * 2 * 32 * 2);  // [NBUF][2][RAW]
+    const int t = threadIdx.x;
+    const long long item = blockIdx.x;
+    const int qp = (int)(item % S);
+    const int h = (int)((item / S) % Hq);
+    const int b = (int)(item / ((long long)S * Hq));
+    const int kvh = h / (Hq / Hkv);
+    const int nqg = (D + qgs - 1) / qgs;
+    const size_t kv_row = (size_t)Hkv * D;
+    const int8_t* Kcb = Kc + b * kc_bstride + (size_t)kvh * D;
+    const int8_t* Vcb = Vc + b * kc_bstride + (size_t)kvh * D;
+    const float* ksb = ks + b * sc_bstride + (size_t)kvh * nqg;
+    const float* vsb = vs + b * sc_bstride + (size_t)kvh * nqg;
+    const __half* Knb = Kn + (size_t)b * new_len * kv_row + (size_t)kvh * D;
+    const __half* Vnb = Vn + (size_t)b * new_len * kv_row + (size_t)kvh * D;
+    const __half* q16 = Q + (((size_t)b * S + qp) * Hq + h) * D;
+    for (int d = t; d < D; d += 256) qs[d] = h2f(q16[d]);
+
+    const long long kv_seq_len = (long long)cache_len + new_len;
+    const long long aq = pos_off + qp;
+    const long long kv_end = causal ? min(kv_seq_len, aq + 1) : kv_seq_len;
+    const int nblk = (int)((kv_end + 31) / 32);
+
+    // issue the cp.async copies of the cached part of block `blk` into buffer `buf`
+    auto prefetch = [&](int blk, int buf) {
+        if (blk < nblk) {
+            const long long b0 = (long long)blk * 32;
+            int8_t* rk = raw + (size_t)buf * 2 * RAW;
+            int8_t* rv = rk + RAW;
+            for (int c = t; c < 32 * (D / 16); c += 256) {
+                const int i = c / (D / 16), off = (c % (D / 16)) * 16;
+                const long long kp = b0 + i;
+                if (kp < cache_len && kp < kv_end) {
+                    cp_async16(rk + i * D + off, Kcb + (size_t)kp * kv_row + off);
+                    cp_async16(rv + i * D + off, Vcb + (size_t)kp * kv_row + off);
+                }
+            }
+            float* rs = rsc + (size_t)buf * 2 * 64;
+            for (int c = t; c < 32 * nqg; c += 256) {
+                const int i = c / nqg, g = c % nqg;
+                const long long kp = b0 + i;
+                if (kp < cache_len && kp < kv_end) {
+                    cp_async4(rs + i * 2 + g, ksb + (size_t)kp * Hkv * nqg + g);
+                    cp_async4(rs + 64 + i * 2 + g, vsb + (size_t)kp * Hkv * nqg + g);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+    prefetch(0, 0);
+    prefetch(1, 1);
+
+    float acc = 0.0f;
+    float run_max = -INFINITY, run_sum = 0.0f;
+    const int ki = t >> 3, kj = t & 7;
+    for (int blk = 0; blk < nblk; ++blk) {
+        prefetch(blk + 2, (blk + 2) % NBUF);
+        cp_async_wait<2>();
+        __syncthreads();
+        const long long b0 = (long long)blk * 32;
+        const int bs = (int)(min(b0 + 32, kv_end) - b0);
+        {  // dequantise block into float tiles (reference: float(int8) * fp32 scale)
+            const int8_t* rk = raw + (size_t)(blk % NBUF) * 2 * RAW;
+            const int8_t* rv = rk + RAW;
+            const float* rs = rsc + (size_t)(blk % NBUF) * 2 * 64;
+            for (int e = t; e < 32 * D; e += 256) {
+                const int i = e / D, d = e % D;
+                const long long kp = b0 + i;
+                float kv = 0.0f, vv = 0.0f;
+                if (i < bs) {
+                    if (kp < cache_len) {
+                        kv = __fmul_rn((float)rk[i * D + d], rs[i * 2 + d / qgs]);
+                        vv = __fmul_rn((float)rv[i * D + d], rs[64 + i * 2 + d / qgs]);
+                    } else {
+                        kv = h2f(Knb[(size_t)(kp - cache_len) * kv_row + d]);
+                        vv = h2f(Vnb[(size_t)(kp - cache_len) * kv_row + d]);
+                    }
+                }
+                kf[i * KS + d] = kv;
+                vf[i * D + d] = vv;
+            }
+        }
+        __syncthreads();
+        // scores: lane kj of key ki's 8-lane dot product, folded in the reference order
+        float a = 0.0f;
+#pragma unroll
+        for (int d = kj; d < D; d += 8) a = fmaf(qs[d], kf[ki * KS + d], a);
+        const int base = (t & 31) & ~7;
+        float p[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) p[m] = __shfl_sync(0xffffffffu, a, base + m);
+        float s = __fmul_rn(fold8(p), scale);
+        const long long kp = b0 + ki;
+        if (ki >= bs || (causal && kp > aq)) s = -INFINITY;
+        if (kj == 0) sc[ki] = s;
+        __syncthreads();
+        float bmax = -INFINITY;
+        for (int i = 0; i < bs; ++i) bmax = fmaxf(bmax, sc[i]);
+        if (bmax > -INFINITY) {
+            const float corr = expf_cr(__fsub_rn(run_max, bmax));
+            run_sum = __fmul_rn(run_sum, corr);
+            acc = __fmul_rn(acc, corr);
+            run_max = bmax;
+        }
+        float w = 0.0f;
+        if (t < bs) w = (sc[t] != -INFINITY) ? expf_cr(__fsub_rn(sc[t], bmax)) : 0.0f;
+        __syncthreads();
+        if (t < 32) sc[t] = w;
+        __syncthreads();
+        float bsum = 0.0f;
+        for (int i = 0; i < bs; ++i) bsum = __fadd_rn(bsum, sc[i]);
+        if (t < D) {
+            for (int i = 0; i < bs; ++i) {
+                const float wi = sc[i];
+                if (wi != 0.0f) acc = fmaf(vf[i * D + t], wi, acc);
+            }
+        }
+        run_sum = __fadd_rn(run_sum, bsum);
+        __syncthreads();
+    }
+    cp_async_wait<0>();
+    __half* o = O + (((size_t)b * S + qp) * Hq + h) * D;
+    if (t < D) o[t] = run_sum > 0.0f ? f2h(__fmul_rn(acc, __fdiv_rn(1.0f, run_sum))) : __float2half_rn(0.0f);
+}
+
+template <int D>
+static size_t exact_smem() {
+    return (size_t)(32 * (D + 8) + 32 * D + D + 32 + 3 * 2 * 32 * 2) * 4 + (size_t)3 * 2 * 32 * D;
+}
+
+int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks,
+                                  const float* vs, const __half* kn, const __half* vn, __half* o, int B, int S,
+                                  int cache_len, int new_len, int Hq, int Hkv, int D, float scale, long long pos_off,
+                                  int causal, int qgs, long long kc_bstride, long long sc_bstride, cudaStream_t st,
+                                  const int* dstate) {
+    const unsigned items = (unsigned)((long long)B * Hq * S);
+#define CB_EXACT(DD)                                                                                          \
+    {                                                                                                         \
+        static bool attr = false;                                                                             \
+        const size_t sm = exact_smem<DD>();                                                                   \
+        if (!attr) {                                                                                          \
+            cudaFuncSetAttribute(attn_hybrid_exact_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                                 (int)sm);                                                                    \
+            attr = true;                                                                                      \
+        }                                                                                                     \
+        attn_hybrid_exact_kernel<DD><<<items, 256, sm, st>>>(q, kc, vc, ks, vs, kn, vn, o, S, cache_len,    \
+                                                             new_len, Hq, Hkv, scale, pos_off, causal, qgs,    \
+                                                             kc_bstride, sc_bstride, dstate);                  \
+        return 0;                                                                                             \
+    }
+    if (qgs % 8 || (D + qgs - 1) / qgs > 2) return -1;
+    switch (D) {
+        case 64: CB_EXACT(64)
+        case 128: CB_EXACT(128)
+        case 256: CB_EXACT(256)
+    }
+#undef CB_EXACT
+    return -1;
+}
+
+void attention_prepare() {
+    cudaFuncSetAttribute(attn_hybrid_exact_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)exact_smem<64>());
+    cudaFuncSetAttribute(attn_hybrid_exact_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)exact_smem<128>());
+    cudaFuncSetAttribute(attn_hybrid_exact_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)exact_smem<256>());
+}
+
 int launch_attention_f16(const __half* q, const __half* k, const __half* v, __half* o, int B, int S, int Skv, int Hq,
                          int Hkv, int D, float scale, long long pos_off, long long window, int causal,
                          cudaStream_t st) {
@@ -242,10 +454,11 @@ int launch_attention_f16(const __half* q, const __half* k, const __half* v, __ha
 int launch_attention_hybrid(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
                             const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len,
                             int Hq, int Hkv, int D, float scale, long long pos_off, int causal, int qgs,
-                            long long kc_bstride, long long sc_bstride, cudaStream_t st) {
+                            long long kc_bstride, long long sc_bstride, cudaStream_t st, const int* dstate) {
     const long long items = (long long)B * Hq * S;
     attn_hybrid_kernel<<<(unsigned)items, 128, 0, st>>>(q, kc, vc, ks, vs, kn, vn, o, B, S, cache_len, new_len, Hq,
-                                                        Hkv, D, scale, pos_off, causal, qgs, kc_bstride, sc_bstride);
+                                                        Hkv, D, scale, pos_off, causal, qgs, kc_bstride, sc_bstride,
+                                                        dstate);
     return 0;
 }
 

@@ -69,6 +69,13 @@ __device__ __forceinline__ float ref_fast_tanh(float x) {
     return r;
 }
 
+// exp / tanh rounded once from the double-precision result: correctly rounded except in
+// vanishingly rare double-rounding cases, so the CPU restatement (which computes the same
+// expression) matches bit for bit. The reference calls libm expf / tanhf, whose results
+// are correctly rounded for all but rare arguments.
+__device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float tanhf_cr(float x) { return (float)tanh((double)x); }
+
 // SiLU of one fp16 value as the vector path of cactus_silu_f16 (kernel_nn.cpp:22-35).
 __device__ __forceinline__ __half ref_silu(__half h) {
     float x = h2f(h);

@@ -1,0 +1,251 @@
+// Device kernels that only the engine uses: fused per-head q/k RMSNorm + RoPE (+ split of
+// the fused QKV projection), KV-cache append, decode-state bookkeeping, embedding lookup,
+// Gemma's norm + clipped residual, and the per-sequence argmax that feeds the next step.
+#include "../common.cuh"
+#include "../gemv.cuh"
+#include "engine_kernels.h"
+
+namespace cb {
+namespace eng {
+
+// ------------------------------------------------------------------ q/k norm + RoPE
+// One warp per (row, head) of the fused projection row [q heads | k heads | v heads].
+// q/k heads: optional per-head RMSNorm (QwenModel::build_attention, model_qwen.cpp:63-70:
+// rms_norm over [seq*heads, head_dim]) then RoPE at position pos_base + (row % S)
+// (cactus_rope_f16, kernel_attention.cpp:614-676); v heads are copied.
+__global__ void __launch_bounds__(128) qkv_post_kernel(QkvPostArgs a) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __half* xs = reinterpret_cast<__half*>(smem_raw) + warp * a.D;
+    const int heads = a.Hq + 2 * a.Hkv;
+    const long long item = (long long)blockIdx.x * 4 + warp;
+    if (item >= (long long)a.rows * heads) return;
+    const int row = (int)(item / heads), hi = (int)(item % heads);
+    const int D = a.D, half = D / 2;
+    const __half* src = a.qkv + (size_t)row * a.qkv_stride + (size_t)hi * D;
+    if (hi >= a.Hq + a.Hkv) {  // value head: copy
+        __half* dst = a.v_out + ((size_t)row * a.Hkv + (hi - a.Hq - a.Hkv)) * D;
+        for (int d = lane; d < D; d += 32) dst[d] = src[d];
+        return;
+    }
+    const bool is_q = hi < a.Hq;
+    const __half* nw = is_q ? a.q_norm : a.k_norm;
+    for (int d = lane; d < D; d += 32) xs[d] = src[d];
+    __syncwarp();
+    if (nw) {
+        const float ss = rms_sumsq_warp(xs, D);
+        const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps));
+        const float inv = __fdiv_rn(1.0f, rms);
+        const __half inv16 = __float2half_rn(inv);
+        const int vec_end = (D / 8) * 8;
+        __syncwarp();
+        for (int d = lane; d < D; d += 32) {
+            const __half v = xs[d];
+            xs[d] = d < vec_end ? __hmul(__hmul(v, inv16), nw[d])
+                                : __float2half_rn(__fmul_rn(__fmul_rn(h2f(v), inv), h2f(nw[d])));
+        }
+        __syncwarp();
+    }
+    const long long pos = (a.dstate ? (long long)a.dstate[1] : a.pos_base) + (row % a.S);
+    __half* dst = is_q ? a.q_out + ((size_t)row * a.Hq + hi) * D : a.k_out + ((size_t)row * a.Hkv + (hi - a.Hq)) * D;
+    if (a.ct == nullptr) {  // rope disabled (rope_theta <= 0)
+        for (int d = lane; d < D; d += 32) dst[d] = xs[d];
+        return;
+    }
+    const __half* c = a.ct + pos * half;
+    const __half* sn = a.st + pos * half;
+    const int vec_half = (half / 8) * 8;
+    for (int i = lane; i < half; i += 32) {
+        const __half x1 = xs[i], x2 = xs[i + half];
+        if (i < vec_half) {
+            dst[i] = __hfma(__hneg(x2), sn[i], __hmul(x1, c[i]));
+            dst[i + half] = __hfma(x1, sn[i], __hmul(x2, c[i]));
+        } else {
+            const float f1 = h2f(x1), f2 = h2f(x2), fc = h2f(c[i]), fs = h2f(sn[i]);
+            dst[i] = f2h(__fsub_rn(__fmul_rn(f1, fc), __fmul_rn(f2, fs)));
+            dst[i + half] = f2h(__fadd_rn(__fmul_rn(f2, fc), __fmul_rn(f1, fs)));
+        }
+    }
+}
+
+// ------------------------------------------------------------------ KV append
+// Quantises tokens [src_tok0, src_tok0 + ntok) of every sequence (fp16 [B, S, Hkv, D]) with
+// the KV rule (kernel_quants.cpp:223-264) into cache slots [dst0, dst0 + ntok) of each
+// sequence's cache ([cap, Hkv, D] int8 + [cap, Hkv, ng] fp32). dst0 comes from the device
+// state (cache_len) when `dstate` is set. One warp per (b, token, head, group).
+__global__ void kv_append_kernel(KvAppendArgs a) {
+    const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int ng = (a.D + a.G - 1) / a.G;
+    const long long total = (long long)a.B * a.ntok * a.Hkv * ng;
+    if (wid >= total) return;
+    const int g = (int)(wid % ng);
+    long long r = wid / ng;
+    const int h = (int)(r % a.Hkv);
+    r /= a.Hkv;
+    const int t = (int)(r % a.ntok);
+    const int b = (int)(r / a.ntok);
+    const long long dst0 = a.dstate ? (long long)a.dstate[0] : a.dst0;
+    const int g0 = g * a.G, cnt = min(a.G, a.D - g0);
+    for (int which = 0; which < 2; ++which) {
+        const __half* src = (which ? a.v_new : a.k_new) +
+                            (((size_t)b * a.S + a.src_tok0 + t) * a.Hkv + h) * a.D + g0;
+        int8_t* dst = (which ? a.v_cache : a.k_cache) + (size_t)b * a.cache_bstride +
+                      ((size_t)(dst0 + t) * a.Hkv + h) * a.D + g0;
+        float* sdst = (which ? a.v_scales : a.k_scales) + (size_t)b * a.scale_bstride +
+                      ((size_t)(dst0 + t) * a.Hkv + h) * ng + g;
+        float mx = 0.0f;
+        for (int k = lane; k < cnt; k += 32) mx = fmaxf(mx, fabsf(h2f(src[k])));
+        mx = warp_max(mx);
+        float scale = __fdiv_rn(mx, 127.0f);
+        if (scale < 1e-10f) scale = 1e-10f;
+        const float inv = __fdiv_rn(1.0f, scale);
+        const int vec = (cnt / 8) * 8;
+        for (int k = lane; k < cnt; k += 32) {
+            const float v = __fmul_rn(h2f(src[k]), inv);
+            dst[k] = (int8_t)sat8(k < vec ? cvt_rne_sat(v) : (int)roundf(v));
+        }
+        if (lane == 0) *sdst = scale;
+    }
+}
+
+// byte copy used for the sliding-window compaction (through a temporary, so overlap is safe)
+__global__ void copy_bytes_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = src[i];
+}
+
+// state[0] = current_seq_len, state[1] = total_seq_len, state[2] = decode step (no sliding)
+__global__ void state_advance_kernel(int* state, int ntok) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        state[0] += ntok;
+        state[1] += ntok;
+        state[2] += 1;
+    }
+}
+
+// ------------------------------------------------------------------ embedding (+ Gemma scale)
+// compute_embedding_node (graph_ops_tensor.cpp:226-331); INT4 tables stay packed and are
+// dequantised per element to the same value as the reference's unpack-then-INT8 path.
+__global__ void embed_kernel(EmbedArgs a) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)a.n * a.hidden) return;
+    const int t = (int)(i / a.hidden), k = (int)(i % a.hidden);
+    const size_t row = a.ids[t];
+    __half v;
+    if (a.prec == 1) {
+        v = reinterpret_cast<const __half*>(a.table)[row * a.hidden + k];
+    } else {
+        int q;
+        if (a.prec == 0) {
+            q = reinterpret_cast<const int8_t*>(a.table)[row * a.hidden + k];
+        } else {
+            const uint8_t byte = reinterpret_cast<const uint8_t*>(a.table)[(row * a.hidden + k) >> 1];
+            q = (k & 1) ? (byte >> 4) : (byte & 0x0F);
+            q = (q & 8) ? q - 16 : q;
+        }
+        v = f2h(__fmul_rn((float)q, h2f(a.scales[row * (a.hidden / a.G) + k / a.G])));
+    }
+    if (a.has_scale) v = __hmul(v, a.scale16);
+    a.out[i] = v;
+}
+
+// ------------------------------------------------------------------ Gemma: hidden = add_clipped(hidden, rms_norm(o))
+// GemmaModel::build_transformer_block (model_gemma.cpp:134-146); one CTA per row.
+__global__ void norm_add_clipped_kernel(__half* __restrict__ hidden, const __half* __restrict__ o,
+                                        const __half* __restrict__ w, int dims, float eps) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __half* xs = reinterpret_cast<__half*>(sm);
+    __shared__ float ssum;
+    const size_t r = blockIdx.x;
+    for (int k = threadIdx.x; k < dims; k += blockDim.x) xs[k] = o[r * dims + k];
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const float ss = rms_sumsq_warp(xs, dims);
+        if (threadIdx.x == 0) ssum = ss;
+    }
+    __syncthreads();
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, (float)dims), eps));
+    const float inv = __fdiv_rn(1.0f, rms);
+    const __half inv16 = __float2half_rn(inv);
+    const int vec_end = dims >= 8 ? (dims / 8) * 8 : 0;
+    for (int k = threadIdx.x; k < dims; k += blockDim.x) {
+        const __half v = xs[k];
+        const __half y = (k < vec_end) ? __hmul(__hmul(v, inv16), w[k])
+                                       : __float2half_rn(__fmul_rn(__fmul_rn(h2f(v), inv), h2f(w[k])));
+        float s = __fadd_rn(h2f(hidden[r * dims + k]), h2f(y));
+        s = fminf(fmaxf(s, -65500.0f), 65500.0f);
+        hidden[r * dims + k] = f2h(s);
+    }
+}
+
+// ------------------------------------------------------------------ per-sequence argmax
+// First maximum wins (kernel_nn.cpp:451-467). Writes the next input token of sequence b and
+// appends it to the output ring at position state[2] (the decode step).
+__global__ void argmax_rows_kernel(const __half* __restrict__ logits, int V, uint32_t* __restrict__ next_tok,
+                                   uint32_t* __restrict__ ring, int ring_stride, const int* __restrict__ state) {
+    __shared__ unsigned long long red[32];
+    const int b = blockIdx.x;
+    const __half* lg = logits + (size_t)b * V;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = h2f(lg[i]);
+        unsigned long long k = 0ull;
+        if (v == v) {
+            unsigned u = __float_as_uint(v);
+            u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            k = ((unsigned long long)u << 32) | (0xFFFFFFFFu - (unsigned)i);
+        }
+        best = k > best ? k : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+            best = k > best ? k : best;
+        }
+        if (threadIdx.x == 0) {
+            const uint32_t tok = best == 0ull ? 0u : 0xFFFFFFFFu - (unsigned)(best & 0xFFFFFFFFull);
+            next_tok[b] = tok;
+            if (ring) ring[(size_t)b * ring_stride + (state ? state[2] : 0)] = tok;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ launchers
+static inline unsigned nb(long long n, int t) { return (unsigned)((n + t - 1) / t); }
+
+void launch_qkv_post(const QkvPostArgs& a, cudaStream_t st) {
+    const long long items = (long long)a.rows * (a.Hq + 2 * a.Hkv);
+    qkv_post_kernel<<<nb(items, 4), 128, 4 * a.D * 2, st>>>(a);
+}
+void launch_kv_append(const KvAppendArgs& a, cudaStream_t st) {
+    const int ng = (a.D + a.G - 1) / a.G;
+    const long long warps = (long long)a.B * a.ntok * a.Hkv * ng;
+    if (warps > 0) kv_append_kernel<<<nb(warps * 32, 256), 256, 0, st>>>(a);
+}
+void launch_copy_bytes(void* dst, const void* src, long long n, cudaStream_t st) {
+    if (n > 0)
+        copy_bytes_kernel<<<nb(n, 256), 256, 0, st>>>(static_cast<uint8_t*>(dst), static_cast<const uint8_t*>(src), n);
+}
+void launch_state_advance(int* state, int ntok, cudaStream_t st) { state_advance_kernel<<<1, 32, 0, st>>>(state, ntok); }
+void launch_embed(const EmbedArgs& a, cudaStream_t st) {
+    embed_kernel<<<nb((long long)a.n * a.hidden, 256), 256, 0, st>>>(a);
+}
+void launch_norm_add_clipped(__half* hidden, const __half* o, const __half* w, int rows, int dims, float eps,
+                             cudaStream_t st) {
+    norm_add_clipped_kernel<<<rows, 256, dims * 2, st>>>(hidden, o, w, dims, eps);
+}
+void launch_argmax_rows(const __half* logits, int rows, int V, uint32_t* next_tok, uint32_t* ring, int ring_stride,
+                        const int* state, cudaStream_t st) {
+    argmax_rows_kernel<<<rows, 1024, 0, st>>>(logits, V, next_tok, ring, ring_stride, state);
+}
+
+}  // namespace eng
+}  // namespace cb

@@ -75,6 +75,23 @@ const char* gemv_check(const GemvCall& c) {
     return nullptr;
 }
 
+// Raises the dynamic shared-memory limit of every GEMV variant once, outside any stream
+// capture (cudaFuncSetAttribute is not a stream operation).
+void gemv_prepare() {
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    for (int wf = 0; wf < 2; ++wf)
+        for (int mt : {1, 2, 4, 8})
+            for (int rpw : {1, 4})
+                for (int ci = 0; ci < kNumCombos; ++ci) {
+                    bool& done = g_attr_set[wf][mt][rpw][ci];
+                    if (done) continue;
+                    KernelFn f = wf ? pick_mt<1>(mt, rpw, ci) : pick_mt<0>(mt, rpw, ci);
+                    if (f && cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) ==
+                                 cudaSuccess)
+                        done = true;
+                }
+}
+
 int launch_gemv(const GemvCall& c, cudaStream_t st) {
     const int mt = c.M <= 1 ? 1 : c.M <= 2 ? 2 : c.M <= 4 ? 4 : 8;
     const int tiles4 = (c.N + 31) / 32;

@@ -124,7 +124,7 @@ __global__ void silu_kernel(const __half* __restrict__ x, __half* __restrict__ y
         y[i] = ref_silu(x[i]);
     } else {
         const float v = h2f(x[i]);
-        y[i] = f2h(__fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)))));
+        y[i] = f2h(__fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-v)))));
     }
 }
 __global__ void gelu_kernel(const __half* __restrict__ x, __half* __restrict__ y, long long n) {
@@ -135,7 +135,7 @@ __global__ void gelu_kernel(const __half* __restrict__ x, __half* __restrict__ y
     } else {
         const float v = h2f(x[i]);
         const float inner = __fmul_rn(0.7978845608028654f, fmaf(__fmul_rn(__fmul_rn(0.044715f, v), v), v, v));
-        y[i] = f2h(__fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner))));
+        y[i] = f2h(__fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf_cr(inner))));
     }
 }
 // op: 0 add, 1 add clipped (fp32 add, clamp +-65500), 2 multiply
@@ -184,7 +184,7 @@ __global__ void softmax_kernel(const __half* __restrict__ x, __half* __restrict_
     const float l2 = __shfl_sync(0xffffffffu, s, 2), l3 = __shfl_sync(0xffffffffu, s, 3);
     float sum = __fadd_rn(__fadd_rn(l0, l1), __fadd_rn(l2, l3));
     for (int i = vv; i < V; ++i) {  // scalar tail, in order (identical on all lanes)
-        const float e = expf(__fsub_rn(h2f(in[i]), mx));
+        const float e = expf_cr(__fsub_rn(h2f(in[i]), mx));
         if (lane == 0) out[i] = f2h(e);
         sum = __fadd_rn(sum, e);
     }

@@ -27,6 +27,7 @@ struct GemvCall {
     bool pdl;  // launch with programmatic stream serialization
 };
 int launch_gemv(const GemvCall& c, cudaStream_t st);
+void gemv_prepare();  // set kernel attributes of all variants (call before graph capture)
 const char* gemv_check(const GemvCall& c);  // nullptr when the shape is supported
 
 // ---- misc (misc.cu)
@@ -55,7 +56,14 @@ int launch_attention_f16(const __half* q, const __half* k, const __half* v, __ha
 int launch_attention_hybrid(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
                             const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len,
                             int Hq, int Hkv, int D, float scale, long long pos_off, int causal, int qgs,
-                            long long kc_bstride, long long sc_bstride, cudaStream_t st);
+                            long long kc_bstride, long long sc_bstride, cudaStream_t st,
+                            const int* dstate = nullptr);
+int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks,
+                                  const float* vs, const __half* kn, const __half* vn, __half* o, int B, int S,
+                                  int cache_len, int new_len, int Hq, int Hkv, int D, float scale, long long pos_off,
+                                  int causal, int qgs, long long kc_bstride, long long sc_bstride, cudaStream_t st,
+                                  const int* dstate = nullptr);
+void attention_prepare();  // kernel attributes, called before any graph capture
 
 // ---- RoPE tables (abi.cu): fp16 cos/sin [n_pos, head_dim/2] built on the host with the
 // reference formula and cached on the current device.

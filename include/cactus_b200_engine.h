@@ -64,6 +64,11 @@ CB_API int cactus_engine_generate_greedy(cactus_engine_t engine, const uint32_t*
 CB_API int cactus_engine_generate_batch_greedy(cactus_engine_t engine, const uint32_t* prompts, size_t batch,
                                                size_t prompt_len, size_t max_new, uint32_t* out_tokens);
 
+/* statistics of the last generate call: out[0] prefill ms, out[1] decode ms (CUDA events on
+ * the engine stream), out[2] kernels launched, out[3] decode-graph replays, out[4] kernel
+ * nodes per replay, out[5] weight bytes in HBM, out[6] KV capacity, out[7] KV window */
+CB_API int cactus_engine_stats(cactus_engine_t engine, double* out8);
+
 /* fp16 logits of the last decoded row of sequence 0 (for parity checks) */
 CB_API int cactus_engine_last_logits(cactus_engine_t engine, uint16_t* host_logits, size_t vocab);
 /* KV state of sequence 0: out[0] = current_seq_len, out[1] = total_seq_len (engine_cache.cpp:101-337) */

@@ -46,6 +46,10 @@ static inline uint16_t hmul(uint16_t a, uint16_t b) { return d2h((double)h2f(a) 
 static inline uint16_t hfma(uint16_t a, uint16_t b, uint16_t c) { /* a*b + c, fused */
     return d2h(fma((double)h2f(a), (double)h2f(b), (double)h2f(c)));
 }
+/* exp / tanh rounded once from double precision (the CUDA path computes the same expression;
+ * both equal a correctly rounded expf/tanhf except in vanishingly rare cases) */
+static inline float expf_cr(float x) { return (float)exp((double)x); }
+static inline float tanhf_cr(float x) { return (float)tanh((double)x); }
 static inline uint32_t fbits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 static inline float bitsf(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
 
@@ -352,7 +356,7 @@ void ref_attention_f16(const uint16_t* Q, const uint16_t* Kc, const uint16_t* V,
                         if (s > bmax) bmax = s;
                     }
                     if (bmax > NINF) {
-                        float corr = expf(run_max - bmax);
+                        float corr = expf_cr(run_max - bmax);
                         run_sum *= corr;
                         for (size_t d = 0; d < hda; ++d) acc[d] *= corr;
                         run_max = bmax;
@@ -366,7 +370,7 @@ void ref_attention_f16(const uint16_t* Q, const uint16_t* Kc, const uint16_t* V,
                         bsum += (y[0] + y[1]) + (y[2] + y[3]);
                     }
                     for (size_t i = vec; i < bs; ++i) {
-                        if (sc[i] != NINF) { sc[i] = expf(sc[i] - bmax); bsum += sc[i]; }
+                        if (sc[i] != NINF) { sc[i] = expf_cr(sc[i] - bmax); bsum += sc[i]; }
                         else sc[i] = 0.0f;
                     }
                     for (size_t i = 0; i < bs; ++i) {
@@ -434,14 +438,14 @@ void ref_attention_hybrid_int8_fp16(const uint16_t* Q, const int8_t* Kc, const i
                         if (s > bmax) bmax = s;
                     }
                     if (bmax > NINF) {
-                        float corr = expf(run_max - bmax);
+                        float corr = expf_cr(run_max - bmax);
                         run_sum *= corr;
                         for (size_t d = 0; d < hda; ++d) acc[d] *= corr;
                         run_max = bmax;
                     }
                     float bsum = 0.0f;
                     for (size_t i = 0; i < bs; ++i) {
-                        if (sc[i] != NINF) { sc[i] = expf(sc[i] - bmax); bsum += sc[i]; }
+                        if (sc[i] != NINF) { sc[i] = expf_cr(sc[i] - bmax); bsum += sc[i]; }
                         else sc[i] = 0.0f;
                     }
                     for (size_t i = 0; i < bs; ++i) {
@@ -505,7 +509,7 @@ void ref_silu_f16(const uint16_t* x, uint16_t* y, size_t n) {
     }
     for (size_t i = vec; i < n; ++i) {
         float v = h2f(x[i]);
-        float sg = 1.0f / (1.0f + expf(-v));
+        float sg = 1.0f / (1.0f + expf_cr(-v));
         y[i] = f2h(v * sg);
     }
 }
@@ -524,7 +528,7 @@ void ref_gelu_f16(const uint16_t* x, uint16_t* y, size_t n) {
     for (size_t i = vec; i < n; ++i) {
         float v = h2f(x[i]);
         float inner = s2p * fmaf((c * v) * v, v, v);
-        y[i] = f2h((0.5f * v) * (1.0f + tanhf(inner)));
+        y[i] = f2h((0.5f * v) * (1.0f + tanhf_cr(inner)));
     }
 }
 
@@ -569,7 +573,7 @@ void ref_softmax_f16(const uint16_t* x, uint16_t* y, size_t rows, size_t V) {
         }
         float sum = (lane[0] + lane[1]) + (lane[2] + lane[3]);
         for (size_t i = vv; i < V; ++i) {
-            float ev = expf(h2f(in[i]) - mx);
+            float ev = expf_cr(h2f(in[i]) - mx);
             out[i] = f2h(ev);
             sum += ev;
         }

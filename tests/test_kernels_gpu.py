@@ -146,8 +146,8 @@ def test_attention_f16_parity(L, ref, B, S, Skv, Hq, Hkv, D, off, win):
     exp = ref.attention(q, k, v, scale, off, win, True)
     got = host(o, np.float16)
     assert rel_err(got, exp) <= TOL
-    # same arithmetic except expf ulps: nearly all fp16 outputs agree bit for bit
-    assert np.mean(got.view(np.uint16) == exp.view(np.uint16)) > 0.95
+    # block partition, quadratic exp, lane orders and online-softmax sequence are reproduced
+    assert same_bits(got, exp)
 
 
 @pytest.mark.parametrize("B,S,L_,Hq,Hkv,D", [(1, 1, 127, 16, 8, 128), (1, 1, 1024, 32, 8, 64),
@@ -166,7 +166,10 @@ def test_attention_hybrid_parity(L, ref, B, S, L_, Hq, Hkv, D):
         ptr(dev(q)), ptr(dev(kc)), ptr(dev(vc)), ptr(dev(ks)), ptr(dev(vs)), ptr(dev(kn)), ptr(dev(vn)), ptr(o),
         B, S, L_, S, Hq, Hkv, D, scale, L_, 1, 128, None))
     exp = ref.attention_hybrid(q, kc[:L_] if L_ else kc[:0], vc[:L_] if L_ else vc[:0], ks, vs, kn, vn, scale, L_)
-    assert rel_err(host(o, np.float16), exp) <= TOL
+    got = host(o, np.float16)
+    assert rel_err(got, exp) <= TOL
+    if L_ + S <= 4096:  # reference-order kernel: bit-exact
+        assert same_bits(got, exp)
 
 
 @pytest.mark.parametrize("S,H,D,G", [(5, 8, 128, 128), (3, 1, 256, 128), (2, 2, 100, 128)])
