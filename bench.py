@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline sample")
     ap.add_argument("--no-kernel-timing", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="only time the GEMV kernel class (one token's projections) and print its roofline")
+    ap.add_argument("--layers", type=int, default=0, help="--kernel-only: number of layers (default: all)")
     return ap.parse_args()
 
 
@@ -128,7 +131,7 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
-def gemv_kernel_timing(arch, dev_index):
+def gemv_kernel_timing(arch, dev_index, layers=0):
     """Times the grouped INT8 GEMV (the dominant kernel: every projection of a decode token)
     with CUDA events around a CUDA graph of one token's 4*28+1 GEMV launches over distinct
     weights (596 MB > L2), launched through the C ABI on torch's stream."""
@@ -138,7 +141,7 @@ def gemv_kernel_timing(arch, dev_index):
     H, F, D, Hq, Hkv = arch.hidden_dim, arch.ffn_intermediate_dim, arch.attention_head_dim, arch.attention_heads, \
         arch.attention_kv_heads
     shapes = []
-    for _ in range(arch.num_layers):
+    for _ in range(layers or arch.num_layers):
         shapes += [((Hq + 2 * Hkv) * D, H), (H, Hq * D), (2 * F, H), (H, F)]
     shapes.append((arch.vocab_size, H))
     g = torch.Generator(device="cuda")
@@ -240,10 +243,27 @@ def run_reference(args):
     return 0
 
 
+def run_kernel_only(args):
+    import torch
+    from cactus_b200 import convert
+    arch = convert.qwen3_0_6b(GROUP)
+    torch.cuda.set_device(0)
+    k = gemv_kernel_timing(arch, 0, args.layers)
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    gbs = k["bytes"] / (k["ms"] / 1e3) / 1e9
+    print(json.dumps({"kernel": "qgemv_kernel", "launches": k["launches"], "bytes": k["bytes"], "ms": k["ms"],
+                      "achieved_gbs": gbs, "frac": gbs / hbm}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernel_only:
+        return run_kernel_only(args)
     import torch
     rank, local_rank, world = dist_env()
     torch.cuda.set_device(local_rank)

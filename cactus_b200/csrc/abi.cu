@@ -339,6 +339,31 @@ CB_API int cactus_cuda_argmax_f16(const uint16_t* logits, size_t rows, size_t vo
     cb::launch_argmax(H(logits) + (rows - 1) * vocab, (int)vocab, out_index, S(stream));
     return check_launch("argmax_f16");
 }
+CB_API int cactus_cuda_sample_f16(const uint16_t* logits, size_t rows, size_t vocab, float temperature, float top_p,
+                                  size_t top_k, float uniform, const uint32_t* history, size_t n_history,
+                                  uint16_t* work, uint32_t* out_index, void* stream) {
+    if (rows == 0 || vocab == 0) return fail(CB_ERR_ARG, "sample: empty logits");
+    const uint16_t* last = logits + (rows - 1) * vocab;
+    if (temperature == 0.0f && top_p <= 0.0f && top_k == 0) {
+        cb::launch_argmax(H(last), (int)vocab, out_index, S(stream));
+        return check_launch("sample_f16");
+    }
+    if (top_p > 0.0f && top_p < 1.0f && (top_k == 0 || top_k > 1000))
+        return fail(CB_ERR_UNSUPPORTED, "sample: top_p filtering needs 0 < top_k <= 1000");
+    if (top_k > 1000 || (top_k == 0 && top_p >= 1.0f && vocab > 1000))
+        return fail(CB_ERR_UNSUPPORTED, "sample: more than 1000 candidates are not supported");
+    if (!work) return fail(CB_ERR_ARG, "sample: scratch buffer required");
+    cb::launch_sample(H(last), (int)vocab, temperature, top_p, (int)top_k, uniform, history, (int)n_history, H(work),
+                      out_index, S(stream));
+    return check_launch("sample_f16");
+}
+
+CB_API int cactus_cuda_entropy_f16(const uint16_t* logits, size_t rows, size_t vocab, float* out, void* stream) {
+    if (rows == 0 || vocab == 0) return fail(CB_ERR_ARG, "entropy: empty logits");
+    cb::launch_entropy(H(logits) + (rows - 1) * vocab, (int)vocab, out, S(stream));
+    return check_launch("entropy_f16");
+}
+
 CB_API int cactus_cuda_unpack_int4_to_int8(const uint8_t* packed, int8_t* unpacked, size_t count, void* stream) {
     if (!count) return CB_OK;
     cb::launch_unpack_int4(packed, unpacked, (long long)count, S(stream));

@@ -253,6 +253,14 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// The online-softmax recurrence of the reference only chains the per-block (max, sum)
+// pair and the per-dim accumulator; scores, block maxima, weights and block sums of a block
+// depend on that block alone. So a chunk of up to 256 keys is processed in phases:
+//   1. all scores in parallel (8-lane dot products in the reference lane order),
+//   2. per 32-key block (one warp each): max, weights expf(s - max), in-order block sum,
+//   3. per output dim (one thread each): walk the blocks in order applying the correction
+//      expf(run_max - block_max) and the in-order V FMAs — the same operation sequence, so
+//      the result is bit-identical, with only the V chain left sequential.
 template <int D>
 __global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
     const __half* __restrict__ Q, const int8_t* __restrict__ Kc, const int8_t* __restrict__ Vc,
@@ -264,17 +272,17 @@ __global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
         cache_len = dstate[0];
         pos_off = dstate[1];
     }
-    constexpr int KS = D + 8;       // padded float stride of the key tile
-    constexpr int RAW = 32 * D;     // bytes of one block of INT8 keys (or values)
-    constexpr int NBUF = 3;
+    constexpr int CH = 256;  // keys per chunk (8 blocks of 32)
     extern __shared__ __align__(16) uint8_t smem[];
-    float* kf = reinterpret_cast<float*>(smem);  // [32][KS]
-    float* vf = kf + 32 * KS;                    // [32][D]
-    float* qs = vf + 32 * D;                     // [D]
-    float* sc = qs + D;                          // [32]
-    float* rsc = sc + 32;                        // raw scales [NBUF][2][32][nqg<=2]
-    int8_t* raw = reinterpret_cast<int8_t*>(rsc + NBUF * 2 * 32 * 2);  // [NBUF][2][RAW]
-    const int t = threadIdx.x;
+    int8_t* kraw = reinterpret_cast<int8_t*>(smem);   // [CH][D]
+    int8_t* vraw = kraw + CH * D;                       // [CH][D]
+    float* qs = reinterpret_cast<float*>(vraw + CH * D);  // [D]
+    float* ksc = qs + D;                                // [CH][2]
+    float* vsc = ksc + CH * 2;                          // [CH][2]
+    float* sc = vsc + CH * 2;                           // [CH] scores, then weights
+    float* bmx = sc + CH;                               // [8]
+    float* bsm = bmx + 8;                               // [8]
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const long long item = blockIdx.x;
     const int qp = (int)(item % S);
     const int h = (int)((item / S) % Hq);
@@ -294,113 +302,99 @@ __global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
     const long long kv_seq_len = (long long)cache_len + new_len;
     const long long aq = pos_off + qp;
     const long long kv_end = causal ? min(kv_seq_len, aq + 1) : kv_seq_len;
-    const int nblk = (int)((kv_end + 31) / 32);
+    float acc = 0.0f, run_max = -INFINITY, run_sum = 0.0f;
 
-    // issue the cp.async copies of the cached part of block `blk` into buffer `buf`
-    auto prefetch = [&](int blk, int buf) {
-        if (blk < nblk) {
-            const long long b0 = (long long)blk * 32;
-            int8_t* rk = raw + (size_t)buf * 2 * RAW;
-            int8_t* rv = rk + RAW;
-            for (int c = t; c < 32 * (D / 16); c += 256) {
-                const int i = c / (D / 16), off = (c % (D / 16)) * 16;
-                const long long kp = b0 + i;
-                if (kp < cache_len && kp < kv_end) {
-                    cp_async16(rk + i * D + off, Kcb + (size_t)kp * kv_row + off);
-                    cp_async16(rv + i * D + off, Vcb + (size_t)kp * kv_row + off);
-                }
-            }
-            float* rs = rsc + (size_t)buf * 2 * 64;
-            for (int c = t; c < 32 * nqg; c += 256) {
-                const int i = c / nqg, g = c % nqg;
-                const long long kp = b0 + i;
-                if (kp < cache_len && kp < kv_end) {
-                    cp_async4(rs + i * 2 + g, ksb + (size_t)kp * Hkv * nqg + g);
-                    cp_async4(rs + 64 + i * 2 + g, vsb + (size_t)kp * Hkv * nqg + g);
-                }
-            }
+    for (long long c0 = 0; c0 < kv_end; c0 += CH) {
+        const int n = (int)min((long long)CH, kv_end - c0);
+        const int ncached = (int)max(0LL, min((long long)n, (long long)cache_len - c0));
+        // stage the cached INT8 rows and scales of this chunk
+        for (int c = t; c < ncached * (D / 16); c += 256) {
+            const int i = c / (D / 16), off = (c % (D / 16)) * 16;
+            const size_t src = (size_t)(c0 + i) * kv_row + off;
+            cp_async16(kraw + i * D + off, Kcb + src);
+            cp_async16(vraw + i * D + off, Vcb + src);
+        }
+        for (int c = t; c < ncached * nqg; c += 256) {
+            const int i = c / nqg, g = c % nqg;
+            cp_async4(ksc + i * 2 + g, ksb + (size_t)(c0 + i) * Hkv * nqg + g);
+            cp_async4(vsc + i * 2 + g, vsb + (size_t)(c0 + i) * Hkv * nqg + g);
         }
         cp_async_commit();
-    };
-    prefetch(0, 0);
-    prefetch(1, 1);
-
-    float acc = 0.0f;
-    float run_max = -INFINITY, run_sum = 0.0f;
-    const int ki = t >> 3, kj = t & 7;
-    for (int blk = 0; blk < nblk; ++blk) {
-        prefetch(blk + 2, (blk + 2) % NBUF);
-        cp_async_wait<2>();
+        cp_async_wait<0>();
         __syncthreads();
-        const long long b0 = (long long)blk * 32;
-        const int bs = (int)(min(b0 + 32, kv_end) - b0);
-        {  // dequantise block into float tiles (reference: float(int8) * fp32 scale)
-            const int8_t* rk = raw + (size_t)(blk % NBUF) * 2 * RAW;
-            const int8_t* rv = rk + RAW;
-            const float* rs = rsc + (size_t)(blk % NBUF) * 2 * 64;
-            for (int e = t; e < 32 * D; e += 256) {
-                const int i = e / D, d = e % D;
-                const long long kp = b0 + i;
-                float kv = 0.0f, vv = 0.0f;
-                if (i < bs) {
-                    if (kp < cache_len) {
-                        kv = __fmul_rn((float)rk[i * D + d], rs[i * 2 + d / qgs]);
-                        vv = __fmul_rn((float)rv[i * D + d], rs[64 + i * 2 + d / qgs]);
-                    } else {
-                        kv = h2f(Knb[(size_t)(kp - cache_len) * kv_row + d]);
-                        vv = h2f(Vnb[(size_t)(kp - cache_len) * kv_row + d]);
-                    }
+        // phase 1: scores (thread = lane kj of key ki's 8-lane dot product)
+        const int kj = t & 7;
+        for (int r = 0; r < CH / 32; ++r) {
+            const int i = (t >> 3) + 32 * r;
+            float a = 0.0f;
+            if (i < n) {
+                if (i < ncached) {
+                    const int8_t* kr = kraw + i * D;
+#pragma unroll
+                    for (int d = kj; d < D; d += 8) a = fmaf(qs[d], __fmul_rn((float)kr[d], ksc[i * 2 + d / qgs]), a);
+                } else {
+                    const __half* kr = Knb + (size_t)(c0 + i - cache_len) * kv_row;
+#pragma unroll
+                    for (int d = kj; d < D; d += 8) a = fmaf(qs[d], h2f(kr[d]), a);
                 }
-                kf[i * KS + d] = kv;
-                vf[i * D + d] = vv;
+            }
+            const int base = lane & ~7;
+            float p[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) p[m] = __shfl_sync(0xffffffffu, a, base + m);
+            float s = __fmul_rn(fold8(p), scale);
+            if (i >= n || (causal && c0 + i > aq)) s = -INFINITY;
+            if (kj == 0 && i < CH) sc[i] = s;
+        }
+        __syncthreads();
+        // phase 2: warp w owns block w of the chunk
+        const int nb = (n + 31) / 32;
+        if (warp < nb) {
+            const int i = warp * 32 + lane;
+            const int bs = min(32, n - warp * 32);
+            const float s = lane < bs ? sc[i] : -INFINITY;
+            const float m = warp_max(s);
+            const float w = (lane < bs && s != -INFINITY) ? expf_cr(__fsub_rn(s, m)) : 0.0f;
+            if (lane < bs) sc[i] = w;
+            float sum = 0.0f;
+            for (int l = 0; l < bs; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, w, l));
+            if (lane == 0) {
+                bmx[warp] = m;
+                bsm[warp] = sum;
             }
         }
         __syncthreads();
-        // scores: lane kj of key ki's 8-lane dot product, folded in the reference order
-        float a = 0.0f;
-#pragma unroll
-        for (int d = kj; d < D; d += 8) a = fmaf(qs[d], kf[ki * KS + d], a);
-        const int base = (t & 31) & ~7;
-        float p[8];
-#pragma unroll
-        for (int m = 0; m < 8; ++m) p[m] = __shfl_sync(0xffffffffu, a, base + m);
-        float s = __fmul_rn(fold8(p), scale);
-        const long long kp = b0 + ki;
-        if (ki >= bs || (causal && kp > aq)) s = -INFINITY;
-        if (kj == 0) sc[ki] = s;
-        __syncthreads();
-        float bmax = -INFINITY;
-        for (int i = 0; i < bs; ++i) bmax = fmaxf(bmax, sc[i]);
-        if (bmax > -INFINITY) {
-            const float corr = expf_cr(__fsub_rn(run_max, bmax));
-            run_sum = __fmul_rn(run_sum, corr);
-            acc = __fmul_rn(acc, corr);
-            run_max = bmax;
-        }
-        float w = 0.0f;
-        if (t < bs) w = (sc[t] != -INFINITY) ? expf_cr(__fsub_rn(sc[t], bmax)) : 0.0f;
-        __syncthreads();
-        if (t < 32) sc[t] = w;
-        __syncthreads();
-        float bsum = 0.0f;
-        for (int i = 0; i < bs; ++i) bsum = __fadd_rn(bsum, sc[i]);
-        if (t < D) {
-            for (int i = 0; i < bs; ++i) {
-                const float wi = sc[i];
-                if (wi != 0.0f) acc = fmaf(vf[i * D + t], wi, acc);
+        // phase 3: the reference's sequential recurrence, one output dim per thread
+        for (int blk = 0; blk < nb; ++blk) {
+            const float m = bmx[blk];
+            if (m > -INFINITY) {
+                const float corr = expf_cr(__fsub_rn(run_max, m));
+                run_sum = __fmul_rn(run_sum, corr);
+                acc = __fmul_rn(acc, corr);
+                run_max = m;
             }
+            if (t < D) {
+                const int i0 = blk * 32, i1 = min(n, i0 + 32);
+                for (int i = i0; i < i1; ++i) {
+                    const float w = sc[i];
+                    if (w == 0.0f) continue;
+                    float v;
+                    if (i < ncached) v = __fmul_rn((float)vraw[i * D + t], vsc[i * 2 + t / qgs]);
+                    else v = h2f(Vnb[(size_t)(c0 + i - cache_len) * kv_row + t]);
+                    acc = fmaf(v, w, acc);
+                }
+            }
+            run_sum = __fadd_rn(run_sum, bsm[blk]);
         }
-        run_sum = __fadd_rn(run_sum, bsum);
         __syncthreads();
     }
-    cp_async_wait<0>();
     __half* o = O + (((size_t)b * S + qp) * Hq + h) * D;
     if (t < D) o[t] = run_sum > 0.0f ? f2h(__fmul_rn(acc, __fdiv_rn(1.0f, run_sum))) : __float2half_rn(0.0f);
 }
 
 template <int D>
 static size_t exact_smem() {
-    return (size_t)(32 * (D + 8) + 32 * D + D + 32 + 3 * 2 * 32 * 2) * 4 + (size_t)3 * 2 * 32 * D;
+    return (size_t)2 * 256 * D + (size_t)(D + 256 * 2 * 2 + 256 + 16) * 4;
 }
 
 int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks,

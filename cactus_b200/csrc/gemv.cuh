@@ -66,10 +66,10 @@ __host__ __device__ inline GemvLayout gemv_layout(int wf, int MT, int RPW, int S
     L.off_act = off;   off += align_up(MT * K, 128);
     L.off_asum = off;  off += align_up(MT * L.ng * 4, 128);
     L.off_as = off;    off += align_up(MT * 4, 16) + 112;
-    L.off_xs = off;    off += (pro == 2) ? align_up(MT * K * 2, 128) : 0;
+    L.off_xs = off;    off += (pro != 0) ? align_up(MT * K * 2, 128) : 0;
     L.off_stage = off; off += S * L.stage_bytes;
     L.off_bar = off;   off += align_up(S * 8, 16) + 16;
-    L.off_gs = off;    off += align_up(kGemvWarps * L.pairs * L.gpj * 4, 16) > 128 ? align_up(kGemvWarps * L.pairs * L.gpj * 4, 16) : 128;
+    L.off_gs = off;    off += align_up(kGemvWarps * L.pairs * L.gpj * 4, 16) > 512 ? align_up(kGemvWarps * L.pairs * L.gpj * 4, 16) : 512;
     off = align_up(off, 16);
     L.off_out = off;   off += 2 * L.R * MT * 2;
     L.total = align_up(off, 128);
@@ -85,6 +85,7 @@ __device__ __forceinline__ float rms_sumsq_warp(const __half* xs, int K) {
     float acc = 0.0f;
     int i = 0;
     const int tile_end = K >= 16 ? K - 16 + 1 : 0;
+#pragma unroll 8
     for (; i < tile_end; i += 16)
         if (lane < 16) { float v = h2f(xs[i + lane]); acc = fmaf(v, v, acc); }
     const int simd_end = K >= 8 ? K - 8 + 1 : 0;
@@ -175,56 +176,59 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
         if (tid < M) as[tid] = a.as[tid];
         __syncthreads();
     } else {
+        // Latency-oriented: one global round trip stages the M rows, warp m reduces row m's
+        // sum of squares, then one pass normalises + takes per-warp maxima and one pass
+        // quantises (3 block barriers for RMSNorm, 2 otherwise).
         __half* xs = reinterpret_cast<__half*>(smem + L.off_xs);
-        float* red = reinterpret_cast<float*>(smem + L.off_gs);  // scratch before the main loop
+        float* red = reinterpret_cast<float*>(smem + L.off_gs);  // [8][8] maxima + [8] sums of squares
+        const int vec_end = (K / 8) * 8;
+        if ((K & 7) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0) {
+            const int4* src = reinterpret_cast<const int4*>(a.x);
+            int4* dst = reinterpret_cast<int4*>(xs);
+            for (int i = tid; i < M * K / 8; i += kGemvThreads) dst[i] = src[i];
+        } else {
+            for (int i = tid; i < M * K; i += kGemvThreads) xs[i] = a.x[i];
+        }
+        __syncthreads();
+        if constexpr (PRO == (int)Pro::RMSNORM_QUANT) {
+            if (warp < M) {
+                const float ss = rms_sumsq_warp(xs + warp * K, K);
+                if (lane == 0) red[64 + warp] = ss;
+            }
+            __syncthreads();
+        }
         for (int m = 0; m < M; ++m) {
-            const __half* xm = a.x + (size_t)m * K;
             float inv_rms = 0.0f;
             __half inv16 = __float2half_rn(0.0f);
             if constexpr (PRO == (int)Pro::RMSNORM_QUANT) {
-                for (int k = tid; k < K; k += kGemvThreads) xs[m * K + k] = xm[k];
-                __syncthreads();
-                if (warp == 0) {
-                    float ss = rms_sumsq_warp(xs + m * K, K);
-                    if (lane == 0) red[0] = ss;
-                }
-                __syncthreads();
-                const float ss = red[0];
-                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps));
+                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(red[64 + m], (float)K), a.eps));
                 inv_rms = __fdiv_rn(1.0f, rms);
                 inv16 = __float2half_rn(inv_rms);
-                __syncthreads();
             }
-            const int vec_end = (K / 8) * 8;
-            // pass 1: (normalize and) absmax
             float mx = 0.0f;
             for (int k = tid; k < K; k += kGemvThreads) {
-                __half v = xm[k];
+                __half v = xs[m * K + k];
                 if constexpr (PRO == (int)Pro::RMSNORM_QUANT) {
-                    __half xv = xs[m * K + k];
-                    v = (k < vec_end) ? __hmul(__hmul(xv, inv16), a.norm_w[k])
-                                      : __float2half_rn(__fmul_rn(__fmul_rn(h2f(xv), inv_rms), h2f(a.norm_w[k])));
+                    v = (k < vec_end) ? __hmul(__hmul(v, inv16), a.norm_w[k])
+                                      : __float2half_rn(__fmul_rn(__fmul_rn(h2f(v), inv_rms), h2f(a.norm_w[k])));
                     xs[m * K + k] = v;
                 }
                 mx = fmaxf(mx, fabsf(h2f(v)));
             }
             mx = warp_max(mx);
-            if (lane == 0) red[warp] = mx;
-            __syncthreads();
-            if (warp == 0) {
-                float v = lane < kGemvWarps ? red[lane] : 0.0f;
-                v = warp_max(v);
-                if (lane == 0) red[16] = v;
-            }
-            __syncthreads();
-            float scale = __fdiv_rn(red[16], 127.0f);
+            if (lane == 0) red[m * 8 + warp] = mx;
+        }
+        __syncthreads();
+        for (int m = 0; m < M; ++m) {
+            float mx = red[m * 8];
+#pragma unroll
+            for (int w = 1; w < kGemvWarps; ++w) mx = fmaxf(mx, red[m * 8 + w]);
+            float scale = __fdiv_rn(mx, 127.0f);
             if (scale < 1e-10f) scale = 1e-10f;
             const float inv = __fdiv_rn(1.0f, scale);
             if (tid == 0) as[m] = scale;
-            // pass 2: quantize
             for (int k = tid; k < K; k += kGemvThreads) {
-                const __half v = (PRO == (int)Pro::RMSNORM_QUANT) ? xs[m * K + k] : xm[k];
-                const int8_t q = quant_act(h2f(v), inv, k < vec_end);
+                const int8_t q = quant_act(h2f(xs[m * K + k]), inv, k < vec_end);
                 if constexpr (WF == 1) {
                     const int blk = k >> 3, e = k & 7;
                     act[m * K + blk * 8 + ((e & 1) ? 4 + (e >> 1) : (e >> 1))] = q;
@@ -234,8 +238,8 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
                 if (a.aq_out && blockIdx.x == 0) a.aq_out[(size_t)m * K + k] = q;
             }
             if (a.as_out && blockIdx.x == 0 && tid == 0) a.as_out[m] = scale;
-            __syncthreads();
         }
+        __syncthreads();
     }
     if constexpr (WF == 1) {  // per-group activation sums for the unsigned-nibble dot product
         for (int i = tid; i < M * ng; i += kGemvThreads) {

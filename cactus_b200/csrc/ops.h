@@ -65,6 +65,11 @@ int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_
                                   const int* dstate = nullptr);
 void attention_prepare();  // kernel attributes, called before any graph capture
 
+// ---- sampling (sample.cu)
+int launch_sample(const __half* logits, int V, float temperature, float top_p, int top_k, float uniform,
+                  const uint32_t* history, int n_history, __half* work, uint32_t* out, cudaStream_t st);
+int launch_entropy(const __half* logits, int V, float* out, cudaStream_t st);
+
 // ---- RoPE tables (abi.cu): fp16 cos/sin [n_pos, head_dim/2] built on the host with the
 // reference formula and cached on the current device.
 bool rope_tables(float theta, int head_dim, long long n_pos, const __half** ct, const __half** st);

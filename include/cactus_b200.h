@@ -128,6 +128,18 @@ CB_API int cactus_cuda_embedding_f16(const uint16_t* table, size_t vocab, size_t
 CB_API int cactus_cuda_argmax_f16(const uint16_t* logits, size_t rows, size_t vocab, uint32_t* out_index,
                                   void* stream);
 
+/* ---- non-greedy sampling: cactus_sample_f16 (kernel_nn.cpp:469-651) on row `rows-1`:
+ *      temperature (fp16 multiply), repetition penalty 1.1 over `history`, top-k, top-p
+ *      (requires 0 < top_k <= 1000 when 0 < top_p < 1), then the first index whose in-order
+ *      cumulative probability reaches `uniform` (the reference draws it from std::mt19937).
+ *      `work` is caller-provided fp16 scratch of `vocab` elements. Greedy arguments
+ *      (temperature 0, top_p <= 0, top_k 0) give the first-max argmax. */
+CB_API int cactus_cuda_sample_f16(const uint16_t* logits, size_t rows, size_t vocab, float temperature, float top_p,
+                                  size_t top_k, float uniform, const uint32_t* history, size_t n_history,
+                                  uint16_t* work, uint32_t* out_index, void* stream);
+/* ---- normalised entropy of softmax(logits[rows-1]) (engine_model.cpp:255-290), fp32 out */
+CB_API int cactus_cuda_entropy_f16(const uint16_t* logits, size_t rows, size_t vocab, float* out, void* stream);
+
 /* ---- INT4 unpack: cactus_unpack_int4_to_int8, kernel_quants.cpp:295-351 */
 CB_API int cactus_cuda_unpack_int4_to_int8(const uint8_t* packed, int8_t* unpacked, size_t count,
                                            void* stream);
