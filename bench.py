@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--kernel-only", action="store_true",
                     help="only time the GEMV kernel class (one token's projections) and print its roofline")
     ap.add_argument("--layers", type=int, default=0, help="--kernel-only: number of layers (default: all)")
+    ap.add_argument("--decode", type=int, default=DECODE, help="decode tokens per request (profiling runs use fewer)")
     return ap.parse_args()
 
 
@@ -260,6 +261,8 @@ def run_kernel_only(args):
 
 def main():
     args = parse()
+    global DECODE
+    DECODE = args.decode
     if args.impl == "reference":
         return run_reference(args)
     if args.kernel_only:

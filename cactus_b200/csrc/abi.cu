@@ -44,6 +44,11 @@ std::map<std::tuple<int, uint32_t, int>, RopeTable> g_rope;  // (device, theta b
 }  // namespace
 
 namespace cb {
+bool& pdl_flag() {
+    static thread_local bool f = false;
+    return f;
+}
+
 // Tables are built with the reference formula (kernel_attention.cpp:580-610):
 // freq_i = 1 / powf(theta, (2i)/head_dim), angle = pos * freq_i, cos/sin rounded to fp16.
 // They only grow (old tables stay allocated) so pointers handed to queued kernels stay valid.
@@ -368,6 +373,13 @@ CB_API int cactus_cuda_unpack_int4_to_int8(const uint8_t* packed, int8_t* unpack
     if (!count) return CB_OK;
     cb::launch_unpack_int4(packed, unpacked, (long long)count, S(stream));
     return check_launch("unpack_int4");
+}
+
+CB_API int cactus_cuda_transpose_2d_f16(const uint16_t* source, uint16_t* destination, size_t num_rows,
+                                        size_t num_cols, void* stream) {
+    if (!source || !destination) return fail(CB_ERR_ARG, "transpose_2d: null pointer");
+    cb::launch_transpose_2d(source, destination, (long long)num_rows, (long long)num_cols, S(stream));
+    return check_launch("transpose_2d_f16");
 }
 
 }  // extern "C"

@@ -29,6 +29,8 @@ __global__ void __launch_bounds__(128) attn_f16_kernel(const __half* __restrict_
                                                        const __half* __restrict__ Vt, __half* __restrict__ O, int B,
                                                        int S, int Skv, int Hq, int Hkv, int D, float scale,
                                                        long long pos_off, long long window, int causal) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float qs[4][kMaxHeadDim];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long item = (long long)blockIdx.x * 4 + warp;  // ((b*Hq + h)*S + q)
@@ -121,6 +123,8 @@ __global__ void __launch_bounds__(128) attn_hybrid_kernel(
     const __half* __restrict__ Vn, __half* __restrict__ O, int B, int S, int cache_len, int new_len, int Hq, int Hkv,
     int D, float scale, long long pos_off, int causal, int qgs, long long kc_bstride, long long sc_bstride,
     const int* __restrict__ dstate) {
+    pdl_launch_dependents();
+    pdl_wait();
     if (dstate) {  // engine decode graphs keep {cache_len, total_len} in device memory
         cache_len = dstate[0];
         pos_off = dstate[1];
@@ -268,6 +272,8 @@ __global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
     const __half* __restrict__ Vn, __half* __restrict__ O, int S, int cache_len, int new_len, int Hq, int Hkv,
     float scale, long long pos_off, int causal, int qgs, long long kc_bstride, long long sc_bstride,
     const int* __restrict__ dstate) {
+    pdl_launch_dependents();
+    pdl_wait();
     if (dstate) {
         cache_len = dstate[0];
         pos_off = dstate[1];
@@ -412,7 +418,7 @@ int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_
                                  (int)sm);                                                                    \
             attr = true;                                                                                      \
         }                                                                                                     \
-        attn_hybrid_exact_kernel<DD><<<items, 256, sm, st>>>(q, kc, vc, ks, vs, kn, vn, o, S, cache_len,    \
+        launch_k(attn_hybrid_exact_kernel<DD>, dim3(items), dim3(256), sm, st, q, kc, vc, ks, vs, kn, vn, o, S, cache_len,    \
                                                              new_len, Hq, Hkv, scale, pos_off, causal, qgs,    \
                                                              kc_bstride, sc_bstride, dstate);                  \
         return 0;                                                                                             \
@@ -440,7 +446,7 @@ int launch_attention_f16(const __half* q, const __half* k, const __half* v, __ha
                          int Hkv, int D, float scale, long long pos_off, long long window, int causal,
                          cudaStream_t st) {
     const long long items = (long long)B * Hq * S;
-    attn_f16_kernel<<<(unsigned)((items + 3) / 4), 128, 0, st>>>(q, k, v, o, B, S, Skv, Hq, Hkv, D, scale, pos_off,
+    launch_k(attn_f16_kernel, dim3((unsigned)((items + 3) / 4)), dim3(128), 0, st, q, k, v, o, B, S, Skv, Hq, Hkv, D, scale, pos_off,
                                                                  window, causal);
     return 0;
 }
@@ -450,7 +456,7 @@ int launch_attention_hybrid(const __half* q, const int8_t* kc, const int8_t* vc,
                             int Hq, int Hkv, int D, float scale, long long pos_off, int causal, int qgs,
                             long long kc_bstride, long long sc_bstride, cudaStream_t st, const int* dstate) {
     const long long items = (long long)B * Hq * S;
-    attn_hybrid_kernel<<<(unsigned)items, 128, 0, st>>>(q, kc, vc, ks, vs, kn, vn, o, B, S, cache_len, new_len, Hq,
+    launch_k(attn_hybrid_kernel, dim3((unsigned)items), dim3(128), 0, st, q, kc, vc, ks, vs, kn, vn, o, B, S, cache_len, new_len, Hq,
                                                         Hkv, D, scale, pos_off, causal, qgs, kc_bstride, sc_bstride,
                                                         dstate);
     return 0;

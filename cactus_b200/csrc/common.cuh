@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace cb {
 
 constexpr int kNumSMs = 148;
@@ -176,6 +178,33 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* gmem_src, unsigned 
 // ---------------------------------------------------------------- programmatic dependent launch
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// Host side: kernels launched through launch_k() get the programmatic-stream-serialization
+// attribute while pdl_scope is active on the calling thread (the engine enables it for its
+// decode/prefill sequences; standalone C-ABI calls run without it, where griddepcontrol.wait
+// is a no-op). Every kernel calls pdl_launch_dependents()/pdl_wait() before touching data
+// produced by earlier launches.
+bool& pdl_flag();
+struct pdl_scope {
+    bool prev;
+    explicit pdl_scope(bool on) : prev(pdl_flag()) { pdl_flag() = on; }
+    ~pdl_scope() { pdl_flag() = prev; }
+};
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_flag() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // 16-byte global load that bypasses L1 allocation (read-only stream)
 __device__ __forceinline__ int4 ldg_nc_v4(const void* p) {

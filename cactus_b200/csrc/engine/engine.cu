@@ -11,8 +11,10 @@
 //   matmul -> add(hidden, .)            = one GEMV with a residual epilogue
 //   gate/up matmuls -> act -> multiply  = one GEMV over row-interleaved gate/up weights
 //   q/k rms_norm -> rope (-> kv quant)  = qkv_post (+ kv_append)
+#include <chrono>
 #include <cmath>
 #include <cstdlib>
+#include <random>
 #include <cstring>
 #include <fstream>
 #include <memory>
@@ -289,6 +291,9 @@ void Engine::init(const std::string& folder, size_t context_size, size_t max_bat
     ids_ = static_cast<uint32_t*>(dmalloc(R * 4, owned_));
     tok_in_ = static_cast<uint32_t*>(dmalloc((size_t)max_batch_ * 4, owned_));
     dstate_ = static_cast<int*>(dmalloc(4 * sizeof(int), owned_));
+    hist_dev_ = static_cast<uint32_t*>(dmalloc(128 * 4, owned_));
+    sample_work_ = static_cast<__half*>(dmalloc((size_t)V_ * 2, owned_));
+    f32_scratch_ = static_cast<float*>(dmalloc(64, owned_));
 
     // RoPE tables per layer (Gemma: global every 6th layer theta 1e6, local 1e4; model_gemma.cpp:84-88)
     ct_.assign(L_, nullptr);
@@ -563,6 +568,7 @@ void Engine::run_forward_tokens(const uint32_t* tokens, int B, int S) {
 // Model::prefill (engine_model.cpp:170-219)
 void Engine::prefill(const uint32_t* tokens, size_t n, size_t chunk) {
     if (n == 0) return;
+    pdl_scope pdl(use_pdl_);
     if (chunk == 0) chunk = 256;
     chunk = std::min(chunk, (size_t)max_rows_);
     if (n <= chunk) {
@@ -586,26 +592,71 @@ void Engine::gather_last(int B, int S) {
     }
 }
 
+// The reference keeps one process-wide repetition-penalty history of the last 128 sampled
+// tokens (kernel_nn.cpp:498-513), appended only on the sampling path.
+static std::mutex g_hist_mu;
+static std::vector<uint32_t> g_history;
+
+// Model::decode (engine_model.cpp:221-297): defaulting rule, forward, lm_head on the last
+// row, optional normalised entropy, then greedy argmax or device sampling with a uniform
+// sample from std::mt19937 seeded by the clock (graph_builder.cpp:408).
 uint32_t Engine::decode(const uint32_t* tokens, size_t n, float temperature, float top_p, size_t top_k, float* entropy) {
     if (temperature < 0) temperature = cfg_.default_temperature;
     if (top_p < 0) top_p = cfg_.default_top_p;
     if (top_k == 0) top_k = cfg_.default_top_k;
     const bool greedy = temperature == 0.0f && top_p <= 0.0f && top_k == 0;
-    if (!greedy) throw std::runtime_error("non-greedy sampling is not implemented by the B200 engine yet");
-    return decode_argmax(tokens, n, entropy);
-}
-
-uint32_t Engine::decode_argmax(const uint32_t* tokens, size_t n, float* entropy) {
+    if (greedy) return decode_argmax(tokens, n, entropy);
+    pdl_scope pdl(use_pdl_);
+    if (top_k > 1000) throw std::runtime_error("top_k above 1000 is not supported by the device sampler");
     if (n == 0) throw std::runtime_error("Token sequence cannot be empty");
     run_forward_tokens(tokens, 1, (int)n);
     gather_last(1, (int)n);
     lm_head(last_, 1);
-    launch_argmax_rows(logits_, 1, V_, tok_in_, nullptr, 0, nullptr, stream_);
+    if (entropy) launch_entropy(logits_, V_, f32_scratch_, stream_);
+    std::vector<uint32_t> hist;
+    {
+        std::lock_guard<std::mutex> lk(g_hist_mu);
+        hist = g_history;
+    }
+    if (!hist.empty())
+        ck(cudaMemcpyAsync(hist_dev_, hist.data(), hist.size() * 4, cudaMemcpyHostToDevice, stream_), "history");
+    std::mt19937 gen((uint32_t)std::chrono::high_resolution_clock::now().time_since_epoch().count());
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+    const float u = dist(gen);
+    launch_sample(logits_, V_, temperature, top_p, (int)top_k, u, hist_dev_, (int)hist.size(), sample_work_,
+                  tok_in_, stream_);
+    launches_ += entropy ? 2 : 1;
     push_state(0);
     uint32_t tok = 0;
+    float ent = 0.0f;
     ck(cudaMemcpyAsync(&tok, tok_in_, 4, cudaMemcpyDeviceToHost, stream_), "token");
+    if (entropy) ck(cudaMemcpyAsync(&ent, f32_scratch_, 4, cudaMemcpyDeviceToHost, stream_), "entropy");
     ck(cudaStreamSynchronize(stream_), "decode");
-    if (entropy) *entropy = 0.0f;
+    if (entropy) *entropy = ent;
+    {
+        std::lock_guard<std::mutex> lk(g_hist_mu);
+        g_history.push_back(tok);
+        if (g_history.size() > 128) g_history.erase(g_history.begin());
+    }
+    return tok;
+}
+
+uint32_t Engine::decode_argmax(const uint32_t* tokens, size_t n, float* entropy) {
+    if (n == 0) throw std::runtime_error("Token sequence cannot be empty");
+    pdl_scope pdl(use_pdl_);
+    run_forward_tokens(tokens, 1, (int)n);
+    gather_last(1, (int)n);
+    lm_head(last_, 1);
+    launch_argmax_rows(logits_, 1, V_, tok_in_, nullptr, 0, nullptr, stream_);
+    if (entropy) launch_entropy(logits_, V_, f32_scratch_, stream_);
+    launches_ += entropy ? 2 : 1;
+    push_state(0);
+    uint32_t tok = 0;
+    float ent = 0.0f;
+    ck(cudaMemcpyAsync(&tok, tok_in_, 4, cudaMemcpyDeviceToHost, stream_), "token");
+    if (entropy) ck(cudaMemcpyAsync(&ent, f32_scratch_, 4, cudaMemcpyDeviceToHost, stream_), "entropy");
+    ck(cudaStreamSynchronize(stream_), "decode");
+    if (entropy) *entropy = ent;
     return tok;
 }
 
@@ -624,6 +675,7 @@ void Engine::generate(const uint32_t* prompts, int B, size_t P, size_t max_new, 
     if (B < 1 || B > max_batch_) throw std::runtime_error("batch exceeds max_batch");
     if (P == 0) throw std::runtime_error("Cannot generate from empty prompt");
     if (max_new == 0) return;
+    pdl_scope pdl(use_pdl_);
     reset();
     check_tokens(prompts, (size_t)B * P);
     if (P + max_new > cap_ + 1) throw std::runtime_error("prompt + max_new exceeds the KV cache capacity");

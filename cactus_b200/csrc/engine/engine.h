@@ -124,7 +124,9 @@ private:
     __half *hidden_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *kall_ = nullptr, *vall_ = nullptr;
     __half *attn_ = nullptr, *tmp_o_ = nullptr, *gated_ = nullptr, *last_ = nullptr, *xnorm_ = nullptr;
     __half* logits_ = nullptr;
-    uint32_t *ids_ = nullptr, *tok_in_ = nullptr, *ring_ = nullptr;
+    uint32_t *ids_ = nullptr, *tok_in_ = nullptr, *ring_ = nullptr, *hist_dev_ = nullptr;
+    __half* sample_work_ = nullptr;
+    float* f32_scratch_ = nullptr;
     size_t ring_cap_ = 0;
     std::vector<const __half*> ct_, st_;
     cudaGraphExec_t graph_exec_ = nullptr;

@@ -14,6 +14,8 @@ namespace eng {
 // rms_norm over [seq*heads, head_dim]) then RoPE at position pos_base + (row % S)
 // (cactus_rope_f16, kernel_attention.cpp:614-676); v heads are copied.
 __global__ void __launch_bounds__(128) qkv_post_kernel(QkvPostArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __half* xs = reinterpret_cast<__half*>(smem_raw) + warp * a.D;
@@ -74,6 +76,8 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(QkvPostArgs a) {
 // sequence's cache ([cap, Hkv, D] int8 + [cap, Hkv, ng] fp32). dst0 comes from the device
 // state (cache_len) when `dstate` is set. One warp per (b, token, head, group).
 __global__ void kv_append_kernel(KvAppendArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int ng = (a.D + a.G - 1) / a.G;
@@ -111,12 +115,16 @@ __global__ void kv_append_kernel(KvAppendArgs a) {
 
 // byte copy used for the sliding-window compaction (through a temporary, so overlap is safe)
 __global__ void copy_bytes_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, long long n) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) dst[i] = src[i];
 }
 
 // state[0] = current_seq_len, state[1] = total_seq_len, state[2] = decode step (no sliding)
 __global__ void state_advance_kernel(int* state, int ntok) {
+    pdl_launch_dependents();
+    pdl_wait();
     if (threadIdx.x == 0 && blockIdx.x == 0) {
         state[0] += ntok;
         state[1] += ntok;
@@ -128,6 +136,8 @@ __global__ void state_advance_kernel(int* state, int ntok) {
 // compute_embedding_node (graph_ops_tensor.cpp:226-331); INT4 tables stay packed and are
 // dequantised per element to the same value as the reference's unpack-then-INT8 path.
 __global__ void embed_kernel(EmbedArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)a.n * a.hidden) return;
     const int t = (int)(i / a.hidden), k = (int)(i % a.hidden);
@@ -154,6 +164,8 @@ __global__ void embed_kernel(EmbedArgs a) {
 // GemmaModel::build_transformer_block (model_gemma.cpp:134-146); one CTA per row.
 __global__ void norm_add_clipped_kernel(__half* __restrict__ hidden, const __half* __restrict__ o,
                                         const __half* __restrict__ w, int dims, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     extern __shared__ __align__(16) uint8_t sm[];
     __half* xs = reinterpret_cast<__half*>(sm);
     __shared__ float ssum;
@@ -184,6 +196,8 @@ __global__ void norm_add_clipped_kernel(__half* __restrict__ hidden, const __hal
 // appends it to the output ring at position state[2] (the decode step).
 __global__ void argmax_rows_kernel(const __half* __restrict__ logits, int V, uint32_t* __restrict__ next_tok,
                                    uint32_t* __restrict__ ring, int ring_stride, const int* __restrict__ state) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ unsigned long long red[32];
     const int b = blockIdx.x;
     const __half* lg = logits + (size_t)b * V;
@@ -223,28 +237,28 @@ static inline unsigned nb(long long n, int t) { return (unsigned)((n + t - 1) / 
 
 void launch_qkv_post(const QkvPostArgs& a, cudaStream_t st) {
     const long long items = (long long)a.rows * (a.Hq + 2 * a.Hkv);
-    qkv_post_kernel<<<nb(items, 4), 128, 4 * a.D * 2, st>>>(a);
+    launch_k(qkv_post_kernel, dim3(nb(items, 4)), dim3(128), 4 * a.D * 2, st, a);
 }
 void launch_kv_append(const KvAppendArgs& a, cudaStream_t st) {
     const int ng = (a.D + a.G - 1) / a.G;
     const long long warps = (long long)a.B * a.ntok * a.Hkv * ng;
-    if (warps > 0) kv_append_kernel<<<nb(warps * 32, 256), 256, 0, st>>>(a);
+    if (warps > 0) launch_k(kv_append_kernel, dim3(nb(warps * 32, 256)), dim3(256), 0, st, a);
 }
 void launch_copy_bytes(void* dst, const void* src, long long n, cudaStream_t st) {
     if (n > 0)
-        copy_bytes_kernel<<<nb(n, 256), 256, 0, st>>>(static_cast<uint8_t*>(dst), static_cast<const uint8_t*>(src), n);
+        launch_k(copy_bytes_kernel, dim3(nb(n, 256)), dim3(256), 0, st, static_cast<uint8_t*>(dst), static_cast<const uint8_t*>(src), n);
 }
-void launch_state_advance(int* state, int ntok, cudaStream_t st) { state_advance_kernel<<<1, 32, 0, st>>>(state, ntok); }
+void launch_state_advance(int* state, int ntok, cudaStream_t st) { launch_k(state_advance_kernel, dim3(1), dim3(32), 0, st, state, ntok); }
 void launch_embed(const EmbedArgs& a, cudaStream_t st) {
-    embed_kernel<<<nb((long long)a.n * a.hidden, 256), 256, 0, st>>>(a);
+    launch_k(embed_kernel, dim3(nb((long long)a.n * a.hidden, 256)), dim3(256), 0, st, a);
 }
 void launch_norm_add_clipped(__half* hidden, const __half* o, const __half* w, int rows, int dims, float eps,
                              cudaStream_t st) {
-    norm_add_clipped_kernel<<<rows, 256, dims * 2, st>>>(hidden, o, w, dims, eps);
+    launch_k(norm_add_clipped_kernel, dim3(rows), dim3(256), dims * 2, st, hidden, o, w, dims, eps);
 }
 void launch_argmax_rows(const __half* logits, int rows, int V, uint32_t* next_tok, uint32_t* ring, int ring_stride,
                         const int* state, cudaStream_t st) {
-    argmax_rows_kernel<<<rows, 1024, 0, st>>>(logits, V, next_tok, ring, ring_stride, state);
+    launch_k(argmax_rows_kernel, dim3(rows), dim3(1024), 0, st, logits, V, next_tok, ring, ring_stride, state);
 }
 
 }  // namespace eng

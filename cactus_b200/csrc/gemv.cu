@@ -43,7 +43,7 @@ KernelFn pick_combo(int ci) {
 }
 template <int WF, int MT>
 KernelFn pick_rpw(int rpw, int ci) {
-    return rpw == 4 ? pick_combo<WF, MT, 4>(ci) : pick_combo<WF, MT, 1>(ci);
+    return rpw == 4 ? pick_combo<WF, MT, 4>(ci) : rpw == 2 ? pick_combo<WF, MT, 2>(ci) : pick_combo<WF, MT, 1>(ci);
 }
 template <int WF>
 KernelFn pick_mt(int mt, int rpw, int ci) {
@@ -81,7 +81,7 @@ void gemv_prepare() {
     std::lock_guard<std::mutex> lk(g_attr_mu);
     for (int wf = 0; wf < 2; ++wf)
         for (int mt : {1, 2, 4, 8})
-            for (int rpw : {1, 4})
+            for (int rpw : {1, 2, 4})
                 for (int ci = 0; ci < kNumCombos; ++ci) {
                     bool& done = g_attr_set[wf][mt][rpw][ci];
                     if (done) continue;
@@ -94,8 +94,9 @@ void gemv_prepare() {
 
 int launch_gemv(const GemvCall& c, cudaStream_t st) {
     const int mt = c.M <= 1 ? 1 : c.M <= 2 ? 2 : c.M <= 4 ? 4 : 8;
-    const int tiles4 = (c.N + 31) / 32;
-    const int rpw = (tiles4 >= 2 * kNumSMs && mt * 4 <= 32) ? 4 : 1;
+    // rows per tile: 8 for narrow outputs (>= 128 tiles at N = 1024), 16 for mid-size, 32 for
+    // very wide ones (the vocabulary projection)
+    const int rpw = c.N >= 32 * 2 * kNumSMs ? 4 : (c.N >= 16 * kNumSMs ? 2 : 1);
     const int R = 8 * rpw;
     const int ntiles = (c.N + R - 1) / R;
     int S = 4;
@@ -145,7 +146,7 @@ int launch_gemv(const GemvCall& c, cudaStream_t st) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = c.pdl ? 1 : 0;
+    cfg.numAttrs = (c.pdl || pdl_flag()) ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, f, a) == cudaSuccess ? 0 : -1;
 }
 

@@ -69,7 +69,7 @@ __host__ __device__ inline GemvLayout gemv_layout(int wf, int MT, int RPW, int S
     L.off_xs = off;    off += (pro != 0) ? align_up(MT * K * 2, 128) : 0;
     L.off_stage = off; off += S * L.stage_bytes;
     L.off_bar = off;   off += align_up(S * 8, 16) + 16;
-    L.off_gs = off;    off += align_up(kGemvWarps * L.pairs * L.gpj * 4, 16) > 512 ? align_up(kGemvWarps * L.pairs * L.gpj * 4, 16) : 512;
+    L.off_gs = off;    off += align_up(L.R * MT * 33 * 4, 16) > 512 ? align_up(L.R * MT * 33 * 4, 16) : 512;
     off = align_up(off, 16);
     L.off_out = off;   off += 2 * L.R * MT * 2;
     L.total = align_up(off, 128);
@@ -252,9 +252,19 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
     }
 
     // ---------------------------------------------------------- main loop over tiles
-    const int chunks = K / 16 / (WF == 1 ? 2 : 1);  // 16-byte weight chunks per row
-    const int npass = (chunks + 31) / 32;
-    const int lanes_per_group = WF == 0 ? G / 16 : G / 32;
+    // Per tile and per slice of 32 groups: (1) warps form the exact int32 group sums of their
+    // rows (lanes split a row's 16-byte chunks, lanes of one group are folded by shuffles)
+    // into gsm[(row*MT + m)*33 + group]; (2) thread t = row*MT + m continues the reference's
+    // sequential fp32 chain over those groups. The padded stride 33 keeps both phases free of
+    // shared-memory bank conflicts.
+    const int cpg = WF == 0 ? G / 16 : G / 32;            // 16-byte weight chunks per group
+    const int chunks = K / 16 / (WF == 1 ? 2 : 1);        // 16-byte chunks per row
+    const int spc = 32 * cpg;                              // chunks per slice of 32 groups
+    const int nslice = (ng + 31) / 32;
+    const int npass = (spc + 31) / 32;
+    int* gsm = reinterpret_cast<int*>(smem + L.off_gs);
+    const int pr = tid / MT, pm = tid % MT;  // chain owner: pair (row pr, activation row pm)
+    const bool chain_thread = tid < R * MT && pm < M;
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int s = it % S;
@@ -270,65 +280,64 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
         uint16_t* ob = outt + (it & 1) * R * MT;
         const int rows_valid = min(R, N - t * R);
 
-        float run0 = 0.0f;
-        const int my_pair = lane;  // owner lane for pair (r, m) = lane
-        const int my_r = my_pair / MT, my_m = my_pair % MT;
-        for (int pass = 0; pass < npass; ++pass) {
-            const int c = pass * 32 + lane;
-            const bool cval = c < chunks;
+        float run = 0.0f;
+        for (int sl = 0; sl < nslice; ++sl) {
+            const int c0 = sl * spc;
+            const int c1 = min(chunks, c0 + spc);
 #pragma unroll
             for (int r = 0; r < RPW; ++r) {
                 const int row = warp * RPW + r;
-                int4 wv = make_int4(0, 0, 0, 0);
-                if (cval && row < rows_valid) wv = *reinterpret_cast<const int4*>(st + row * L.wrow + c * 16);
+                for (int p = 0; p < npass; ++p) {
+                    const int c = c0 + p * 32 + lane;
+                    const bool cval = c < c1;
+                    int4 wv = make_int4(0, 0, 0, 0);
+                    if (cval && row < rows_valid) wv = *reinterpret_cast<const int4*>(st + row * L.wrow + c * 16);
 #pragma unroll
-                for (int m = 0; m < MT; ++m) {
-                    int acc = 0;
-                    if (cval && m < M) {
-                        if constexpr (WF == 0) {
-                            const int4 av = *reinterpret_cast<const int4*>(act + m * K + c * 16);
-                            acc = dp4a_ss(av.x, wv.x, acc);
-                            acc = dp4a_ss(av.y, wv.y, acc);
-                            acc = dp4a_ss(av.z, wv.z, acc);
-                            acc = dp4a_ss(av.w, wv.w, acc);
-                        } else {
-                            const int4 a0 = *reinterpret_cast<const int4*>(act + m * K + c * 32);
-                            const int4 a1 = *reinterpret_cast<const int4*>(act + m * K + c * 32 + 16);
-                            const unsigned ww[4] = {(unsigned)wv.x, (unsigned)wv.y, (unsigned)wv.z, (unsigned)wv.w};
-                            const int ae[4] = {a0.x, a0.z, a1.x, a1.z};
-                            const int ao[4] = {a0.y, a0.w, a1.y, a1.w};
+                    for (int m = 0; m < MT; ++m) {
+                        int acc = 0;
+                        if (cval && m < M) {
+                            if constexpr (WF == 0) {
+                                const int4 av = *reinterpret_cast<const int4*>(act + m * K + c * 16);
+                                acc = dp4a_ss(av.x, wv.x, acc);
+                                acc = dp4a_ss(av.y, wv.y, acc);
+                                acc = dp4a_ss(av.z, wv.z, acc);
+                                acc = dp4a_ss(av.w, wv.w, acc);
+                            } else {
+                                const int4 a0 = *reinterpret_cast<const int4*>(act + m * K + c * 32);
+                                const int4 a1 = *reinterpret_cast<const int4*>(act + m * K + c * 32 + 16);
+                                const unsigned ww[4] = {(unsigned)wv.x, (unsigned)wv.y, (unsigned)wv.z,
+                                                        (unsigned)wv.w};
+                                const int ae[4] = {a0.x, a0.z, a1.x, a1.z};
+                                const int ao[4] = {a0.y, a0.w, a1.y, a1.w};
 #pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const unsigned lo = (ww[q] & 0x0F0F0F0Fu) ^ 0x08080808u;
-                                const unsigned hi = ((ww[q] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
-                                acc = dp4a_su(ae[q], lo, acc);
-                                acc = dp4a_su(ao[q], hi, acc);
+                                for (int q = 0; q < 4; ++q) {
+                                    const unsigned lo = (ww[q] & 0x0F0F0F0Fu) ^ 0x08080808u;
+                                    const unsigned hi = ((ww[q] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+                                    acc = dp4a_su(ae[q], lo, acc);
+                                    acc = dp4a_su(ao[q], hi, acc);
+                                }
                             }
                         }
-                    }
-                    for (int o = 1; o < lanes_per_group; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                    if ((lane % lanes_per_group) == 0 && cval) {
-                        const int g = (WF == 0 ? c * 16 : c * 32) / G;
-                        if constexpr (WF == 1) acc -= 8 * asum[m * ng + g];
-                        gsbuf[(r * MT + m) * L.gpj + (g - pass * L.gpj)] = acc;
+                        for (int o = 1; o < cpg; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                        if ((lane % cpg) == 0 && cval) {
+                            const int gl = (c - c0) / cpg;
+                            if constexpr (WF == 1) acc -= 8 * asum[m * ng + sl * 32 + gl];
+                            gsm[(row * MT + m) * 33 + gl] = acc;
+                        }
                     }
                 }
             }
-            __syncwarp();
-            if (my_pair < L.pairs) {
-                const int row = warp * RPW + my_r;
-                const int g0 = pass * L.gpj;
-                const int g1 = min(ng, g0 + L.gpj);
-                const int* gs = gsbuf + my_pair * L.gpj;
-                for (int g = g0; g < g1; ++g)
-                    run0 = fmaf((float)gs[g - g0], h2f_bits(sc[row * ng + g]), run0);
+            __syncthreads();
+            if (chain_thread) {
+                const int gcount = min(32, ng - sl * 32);
+                const int* gp = gsm + tid * 33;
+                const uint16_t* sp = sc + pr * ng + sl * 32;
+#pragma unroll 8
+                for (int gl = 0; gl < gcount; ++gl) run = fmaf((float)gp[gl], h2f_bits(sp[gl]), run);
             }
-            __syncwarp();
+            __syncthreads();
         }
-        if (my_pair < L.pairs) {
-            const int row = warp * RPW + my_r;
-            if (my_m < M) ob[row * MT + my_m] = f2h_bits(__fmul_rn(run0, as[my_m]));
-        }
+        if (chain_thread) ob[pr * MT + pm] = f2h_bits(__fmul_rn(run, as[pm]));
         __syncthreads();
         if (tid == 0) {
             const int tn = t + S * (int)gridDim.x;

@@ -13,6 +13,8 @@ __device__ unsigned g_dev_error = 0;
 // graph_ops_nn.cpp:35-66: per row absmax -> scale = max(absmax/127, 1e-10) -> int8 (RNE).
 __global__ void quantize_act_kernel(const __half* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scales,
                                     int K) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int m = blockIdx.x;
     const __half* xm = x + (size_t)m * K;
     __shared__ float red[33];
@@ -38,6 +40,8 @@ __global__ void quantize_act_kernel(const __half* __restrict__ x, int8_t* __rest
 // ------------------------------------------------------------------ RMSNorm (kernel_attention.cpp:484-563)
 __global__ void rms_norm_kernel(const __half* __restrict__ x, const __half* __restrict__ w, __half* __restrict__ y,
                                 int dims, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     extern __shared__ __align__(16) uint8_t sm[];
     __half* xs = reinterpret_cast<__half*>(sm);
     __shared__ float ssum;
@@ -66,6 +70,8 @@ __global__ void rms_norm_kernel(const __half* __restrict__ x, const __half* __re
 __global__ void rope_kernel(const __half* __restrict__ in, __half* __restrict__ out, const __half* __restrict__ ct,
                             const __half* __restrict__ st, long long total_pairs, int seq_len, int num_heads,
                             int head_dim, long long start_pos) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= total_pairs) return;
     const int half = head_dim / 2;
@@ -92,6 +98,8 @@ __global__ void rope_kernel(const __half* __restrict__ in, __half* __restrict__ 
 // One warp per (token*head, group): absmax -> scale -> RNE quantisation of the vector part.
 __global__ void quantize_kv_kernel(const __half* __restrict__ src, int8_t* __restrict__ dst, float* __restrict__ scales,
                                    long long rows, int head_dim, int G) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int ng = (head_dim + G - 1) / G;
     const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -118,6 +126,8 @@ __global__ void quantize_kv_kernel(const __half* __restrict__ src, int8_t* __res
 // ------------------------------------------------------------------ elementwise
 // Vector-path semantics for the first (n/8)*8 elements, scalar-tail semantics after.
 __global__ void silu_kernel(const __half* __restrict__ x, __half* __restrict__ y, long long n) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     if (i < (n / 8) * 8) {
@@ -128,6 +138,8 @@ __global__ void silu_kernel(const __half* __restrict__ x, __half* __restrict__ y
     }
 }
 __global__ void gelu_kernel(const __half* __restrict__ x, __half* __restrict__ y, long long n) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     if (i < (n / 8) * 8) {
@@ -141,6 +153,8 @@ __global__ void gelu_kernel(const __half* __restrict__ x, __half* __restrict__ y
 // op: 0 add, 1 add clipped (fp32 add, clamp +-65500), 2 multiply
 __global__ void binary_kernel(const __half* __restrict__ a, const __half* __restrict__ b, __half* __restrict__ y,
                               long long n, int op) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     if (op == 0) {
@@ -154,6 +168,8 @@ __global__ void binary_kernel(const __half* __restrict__ a, const __half* __rest
     }
 }
 __global__ void scalar_mul_kernel(const __half* __restrict__ x, __half* __restrict__ y, long long n, __half s) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = __hmul(x[i], s);
 }
@@ -162,6 +178,8 @@ __global__ void scalar_mul_kernel(const __half* __restrict__ x, __half* __restri
 // One warp per row. Lane e owns the reference's accumulator for offset e of every 32-wide
 // chunk, so the fp32 sum follows the NEON lane order exactly.
 __global__ void softmax_kernel(const __half* __restrict__ x, __half* __restrict__ y, int rows, int V) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -199,6 +217,8 @@ __global__ void softmax_kernel(const __half* __restrict__ x, __half* __restrict_
 __global__ void embedding_int8_kernel(const int8_t* __restrict__ table, const __half* __restrict__ scales, int G,
                                       int ng, int hidden, const uint32_t* __restrict__ ids, int n_ids,
                                       __half* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)n_ids * hidden) return;
     const int t = (int)(i / hidden), k = (int)(i % hidden);
@@ -207,6 +227,8 @@ __global__ void embedding_int8_kernel(const int8_t* __restrict__ table, const __
 }
 __global__ void embedding_f16_kernel(const __half* __restrict__ table, int hidden, const uint32_t* __restrict__ ids,
                                      int n_ids, __half* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)n_ids * hidden) return;
     const int t = (int)(i / hidden), k = (int)(i % hidden);
@@ -222,6 +244,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, unsigned idx) 
     return ((unsigned long long)u << 32) | (0xFFFFFFFFu - idx);
 }
 __global__ void argmax_kernel(const __half* __restrict__ logits, int V, uint32_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ unsigned long long red[32];
     unsigned long long best = 0ull;
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
@@ -246,11 +270,33 @@ __global__ void argmax_kernel(const __half* __restrict__ logits, int V, uint32_t
 
 // ------------------------------------------------------------------ INT4 unpack (kernel_quants.cpp:295-351)
 __global__ void unpack_int4_kernel(const uint8_t* __restrict__ p, int8_t* __restrict__ o, long long count) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= count) return;
     const uint8_t b = p[i >> 1];
     int v = (i & 1) ? (b >> 4) : (b & 0x0F);
     o[i] = (int8_t)((v & 8) ? v - 16 : v);
+}
+
+// ------------------------------------------------------------------ 2-D transpose (kernel_blas.cpp:407-493)
+// 32x32 tiles through shared memory (one padding column against bank conflicts); rows and
+// columns both read and written coalesced.
+__global__ void transpose_2d_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, long long rows,
+                                    long long cols) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ uint16_t tile[32][33];
+    const long long r0 = (long long)blockIdx.y * 32, c0 = (long long)blockIdx.x * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const long long r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[i][threadIdx.x] = src[r * cols + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const long long c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) dst[c * rows + r] = tile[threadIdx.x][i];
+    }
 }
 
 // ------------------------------------------------------------------ FP16 matmul (kernel_gemm.cpp:17-126)
@@ -259,6 +305,8 @@ __global__ void unpack_int4_kernel(const uint8_t* __restrict__ p, int8_t* __rest
 // reference's fp16 horizontal-sum tree (kernel_gemm.cpp:8-15).
 __global__ void matmul_f16_kernel(const __half* __restrict__ A, const __half* __restrict__ Bt, __half* __restrict__ C,
                                   int M, int K, int N) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int j = threadIdx.x & 7;
     const long long n = (long long)blockIdx.x * (blockDim.x >> 3) + (threadIdx.x >> 3);
     const bool valid = n < N;
@@ -292,66 +340,73 @@ namespace cb {
 static inline unsigned nblocks(long long n, int t) { return (unsigned)((n + t - 1) / t); }
 
 int launch_quantize_act(const __half* x, int8_t* q, float* s, int M, int K, cudaStream_t st) {
-    quantize_act_kernel<<<M, 256, 0, st>>>(x, q, s, K);
+    launch_k(quantize_act_kernel, dim3(M), dim3(256), 0, st, x, q, s, K);
     return 0;
 }
 int launch_rms_norm(const __half* x, const __half* w, __half* y, int rows, int dims, float eps, cudaStream_t st) {
     const size_t sm = (size_t)dims * 2;
     if (sm > 48 * 1024) cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    rms_norm_kernel<<<rows, 256, sm, st>>>(x, w, y, dims, eps);
+    launch_k(rms_norm_kernel, dim3(rows), dim3(256), sm, st, x, w, y, dims, eps);
     return 0;
 }
 int launch_rope(const __half* in, __half* out, const __half* ct, const __half* stab, long long rows, int seq_len,
                 int heads, int head_dim, long long start_pos, cudaStream_t st) {
     const long long pairs = rows * (head_dim / 2);
-    rope_kernel<<<nblocks(pairs, 256), 256, 0, st>>>(in, out, ct, stab, pairs, seq_len, heads, head_dim, start_pos);
+    launch_k(rope_kernel, dim3(nblocks(pairs, 256)), dim3(256), 0, st, in, out, ct, stab, pairs, seq_len, heads, head_dim, start_pos);
     return 0;
 }
 int launch_quantize_kv(const __half* src, int8_t* dst, float* scales, long long rows, int head_dim, int G,
                        cudaStream_t st) {
     const int ng = (head_dim + G - 1) / G;
-    quantize_kv_kernel<<<nblocks(rows * ng * 32, 256), 256, 0, st>>>(src, dst, scales, rows, head_dim, G);
+    launch_k(quantize_kv_kernel, dim3(nblocks(rows * ng * 32, 256)), dim3(256), 0, st, src, dst, scales, rows, head_dim, G);
     return 0;
 }
 int launch_silu(const __half* x, __half* y, long long n, cudaStream_t st) {
-    silu_kernel<<<nblocks(n, 256), 256, 0, st>>>(x, y, n);
+    launch_k(silu_kernel, dim3(nblocks(n, 256)), dim3(256), 0, st, x, y, n);
     return 0;
 }
 int launch_gelu(const __half* x, __half* y, long long n, cudaStream_t st) {
-    gelu_kernel<<<nblocks(n, 256), 256, 0, st>>>(x, y, n);
+    launch_k(gelu_kernel, dim3(nblocks(n, 256)), dim3(256), 0, st, x, y, n);
     return 0;
 }
 int launch_binary(const __half* a, const __half* b, __half* y, long long n, int op, cudaStream_t st) {
-    binary_kernel<<<nblocks(n, 256), 256, 0, st>>>(a, b, y, n, op);
+    launch_k(binary_kernel, dim3(nblocks(n, 256)), dim3(256), 0, st, a, b, y, n, op);
     return 0;
 }
 int launch_scalar_mul(const __half* x, __half* y, long long n, float s, cudaStream_t st) {
-    scalar_mul_kernel<<<nblocks(n, 256), 256, 0, st>>>(x, y, n, __float2half_rn(s));
+    launch_k(scalar_mul_kernel, dim3(nblocks(n, 256)), dim3(256), 0, st, x, y, n, __float2half_rn(s));
     return 0;
 }
 int launch_softmax(const __half* x, __half* y, int rows, int V, cudaStream_t st) {
-    softmax_kernel<<<nblocks((long long)rows * 32, 128), 128, 0, st>>>(x, y, rows, V);
+    launch_k(softmax_kernel, dim3(nblocks((long long)rows * 32, 128)), dim3(128), 0, st, x, y, rows, V);
     return 0;
 }
 int launch_embedding_int8(const int8_t* t, const __half* s, int G, int hidden, const uint32_t* ids, int n,
                           __half* out, cudaStream_t st) {
-    embedding_int8_kernel<<<nblocks((long long)n * hidden, 256), 256, 0, st>>>(t, s, G, hidden / G, hidden, ids, n, out);
+    launch_k(embedding_int8_kernel, dim3(nblocks((long long)n * hidden, 256)), dim3(256), 0, st, t, s, G, hidden / G, hidden, ids, n, out);
     return 0;
 }
 int launch_embedding_f16(const __half* t, int hidden, const uint32_t* ids, int n, __half* out, cudaStream_t st) {
-    embedding_f16_kernel<<<nblocks((long long)n * hidden, 256), 256, 0, st>>>(t, hidden, ids, n, out);
+    launch_k(embedding_f16_kernel, dim3(nblocks((long long)n * hidden, 256)), dim3(256), 0, st, t, hidden, ids, n, out);
     return 0;
 }
 int launch_argmax(const __half* logits, int V, uint32_t* out, cudaStream_t st) {
-    argmax_kernel<<<1, 1024, 0, st>>>(logits, V, out);
+    launch_k(argmax_kernel, dim3(1), dim3(1024), 0, st, logits, V, out);
     return 0;
 }
+int launch_transpose_2d(const uint16_t* src, uint16_t* dst, long long rows, long long cols, cudaStream_t st) {
+    if (rows == 0 || cols == 0) return 0;
+    launch_k(transpose_2d_kernel, dim3((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32)), dim3(32, 8), 0, st,
+             src, dst, rows, cols);
+    return 0;
+}
+
 int launch_unpack_int4(const uint8_t* p, int8_t* o, long long count, cudaStream_t st) {
-    unpack_int4_kernel<<<nblocks(count, 256), 256, 0, st>>>(p, o, count);
+    launch_k(unpack_int4_kernel, dim3(nblocks(count, 256)), dim3(256), 0, st, p, o, count);
     return 0;
 }
 int launch_matmul_f16(const __half* A, const __half* Bt, __half* C, int M, int K, int N, cudaStream_t st) {
-    matmul_f16_kernel<<<nblocks((long long)N * 8, 256), 256, 0, st>>>(A, Bt, C, M, K, N);
+    launch_k(matmul_f16_kernel, dim3(nblocks((long long)N * 8, 256)), dim3(256), 0, st, A, Bt, C, M, K, N);
     return 0;
 }
 

@@ -47,6 +47,7 @@ int launch_embedding_int8(const int8_t* t, const __half* s, int G, int hidden, c
 int launch_embedding_f16(const __half* t, int hidden, const uint32_t* ids, int n, __half* out, cudaStream_t st);
 int launch_argmax(const __half* logits, int V, uint32_t* out, cudaStream_t st);
 int launch_unpack_int4(const uint8_t* p, int8_t* o, long long count, cudaStream_t st);
+int launch_transpose_2d(const uint16_t* src, uint16_t* dst, long long rows, long long cols, cudaStream_t st);
 int launch_matmul_f16(const __half* A, const __half* Bt, __half* C, int M, int K, int N, cudaStream_t st);
 
 // ---- attention (attention.cu)

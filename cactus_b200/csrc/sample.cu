@@ -42,6 +42,8 @@ struct SampleArgs {
 };
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ unsigned hist[256];
     __shared__ unsigned sel_hi, sel_lo, need;
     __shared__ float cval[kMaxCand];
@@ -198,6 +200,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
 
 // normalised entropy of softmax(logits) in double precision (engine_model.cpp:255-290)
 __global__ void __launch_bounds__(1024) entropy_kernel(const __half* __restrict__ logits, int V, float* out) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ double red[32];
     __shared__ float fmx;
     const int t = threadIdx.x;
@@ -255,12 +259,12 @@ int launch_sample(const __half* logits, int V, float temperature, float top_p, i
     a.n_history = n_history;
     a.work = work;
     a.out = out;
-    sample_kernel<<<1, kSampleThreads, 0, st>>>(a);
+    launch_k(sample_kernel, dim3(1), dim3(kSampleThreads), 0, st, a);
     return 0;
 }
 
 int launch_entropy(const __half* logits, int V, float* out, cudaStream_t st) {
-    entropy_kernel<<<1, 1024, 0, st>>>(logits, V, out);
+    launch_k(entropy_kernel, dim3(1), dim3(1024), 0, st, logits, V, out);
     return 0;
 }
 

@@ -144,6 +144,11 @@ CB_API int cactus_cuda_entropy_f16(const uint16_t* logits, size_t rows, size_t v
 CB_API int cactus_cuda_unpack_int4_to_int8(const uint8_t* packed, int8_t* unpacked, size_t count,
                                            void* stream);
 
+/* ---- 2-D transpose: cactus_transpose_2d_f16, kernel_blas.cpp:407-493 (whole matrix).
+ *      source [num_rows, num_cols] -> destination [num_cols, num_rows]. */
+CB_API int cactus_cuda_transpose_2d_f16(const uint16_t* source, uint16_t* destination, size_t num_rows,
+                                        size_t num_cols, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
