@@ -220,7 +220,7 @@ CB_API int cactus_cuda_rope_f16(const uint16_t* input, uint16_t* output, size_t 
 
 static const char* attn_dims_check(size_t Hq, size_t Hkv, size_t D) {
     if (Hq == 0 || Hkv == 0 || Hq % Hkv) return "num_q_heads must be a positive multiple of num_kv_heads";
-    if (D == 0 || D % 32 || D > 256) return "head_dim must be a multiple of 32 and <= 256";
+    if (D == 0 || D > 256) return "head_dim must be in [1, 256]";
     return nullptr;
 }
 
@@ -250,6 +250,7 @@ CB_API int cactus_cuda_attention_hybrid_int8_fp16(const uint16_t* queries, const
     if (batch_size == 0 || seq_len == 0) return CB_OK;
     if (const char* why = attn_dims_check(num_q_heads, num_kv_heads, head_dim))
         return fail(CB_ERR_ARG, std::string("attention_hybrid: ") + why);
+    if (head_dim % 32) return fail(CB_ERR_UNSUPPORTED, "attention_hybrid: head_dim must be a multiple of 32");
     if (quant_group_size == 0 || quant_group_size % 8) return fail(CB_ERR_ARG, "attention_hybrid: bad quant group");
     if (!aligned16(keys_new) || !aligned16(values_new) || (reinterpret_cast<uintptr_t>(keys_cached) & 7) ||
         (reinterpret_cast<uintptr_t>(values_cached) & 7))

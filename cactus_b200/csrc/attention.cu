@@ -11,6 +11,7 @@
 //
 // Scores use the reference's 8-lane fp32 dot-product order (accumulator j sums dims
 // d = j mod 8 with FMAs, folded as ((a0+a4)+(a1+a5))+((a2+a6)+(a3+a7))).
+#include "attention_core.cuh"
 #include "common.cuh"
 #include "ops.h"
 
@@ -18,13 +19,10 @@ namespace cb {
 
 constexpr int kMaxHeadDim = 256;
 
-__device__ __forceinline__ float fold8(const float* a) {
-    return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[1], a[5])),
-                     __fadd_rn(__fadd_rn(a[2], a[6]), __fadd_rn(a[3], a[7])));
-}
 
-// One warp per (batch, q head, query). Lane i scores key i of each 32-key block; lanes own
-// head_dim/32 output dims for the value accumulation.
+// One warp per (batch, q head, query). Lane i scores key i of each 32-key block; lane l owns
+// output dims l, l+32, ... for the value accumulation. As in the reference, dims past the last
+// multiple of 8 (head_dim_aligned) only enter the scores; their outputs are zero.
 __global__ void __launch_bounds__(128) attn_f16_kernel(const __half* __restrict__ Q, const __half* __restrict__ Kt,
                                                        const __half* __restrict__ Vt, __half* __restrict__ O, int B,
                                                        int S, int Skv, int Hq, int Hkv, int D, float scale,
@@ -43,7 +41,8 @@ __global__ void __launch_bounds__(128) attn_f16_kernel(const __half* __restrict_
     __half* o = O + (((size_t)b * S + qp) * Hq + h) * D;
     for (int d = lane; d < D; d += 32) qs[warp][d] = h2f(q16[d]);
     __syncwarp();
-    const int dpl = D / 32;  // dims per lane
+    const int dpl = (D + 31) / 32;  // dims per lane
+    const int hda = (D / 8) * 8;
     float acc[kMaxHeadDim / 32];
 #pragma unroll
     for (int i = 0; i < kMaxHeadDim / 32; ++i) acc[i] = 0.0f;
@@ -68,13 +67,21 @@ __global__ void __launch_bounds__(128) attn_f16_kernel(const __half* __restrict_
         if (lane < bs && !(!is_decode && causal && kp > aq)) {
             const __half* kr = Kb + (size_t)kp * kv_row;
             float a8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int d = 0; d < D; d += 8) {
-                const int4 kv4 = *reinterpret_cast<const int4*>(kr + d);
-                const __half* kh = reinterpret_cast<const __half*>(&kv4);
+            if ((D & 7) == 0) {
+                for (int d = 0; d < D; d += 8) {
+                    const int4 kv4 = *reinterpret_cast<const int4*>(kr + d);
+                    const __half* kh = reinterpret_cast<const __half*>(&kv4);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) a8[j] = fmaf(qs[warp][d + j], h2f(kh[j]), a8[j]);
+                    for (int j = 0; j < 8; ++j) a8[j] = fmaf(qs[warp][d + j], h2f(kh[j]), a8[j]);
+                }
+            } else {
+                for (int d = 0; d < hda; d += 8)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) a8[j] = fmaf(qs[warp][d + j], h2f(kr[d + j]), a8[j]);
             }
-            s = __fmul_rn(fold8(a8), scale);
+            float dot = fold8(a8);
+            for (int d = hda; d < D; ++d) dot = fmaf(qs[warp][d], h2f(kr[d]), dot);
+            s = __fmul_rn(dot, scale);
             if (causal && kp > aq) s = -INFINITY;
             else if (window > 0 && kp < aq && (aq - kp) > window) s = -INFINITY;
         }
@@ -100,15 +107,15 @@ __global__ void __launch_bounds__(128) attn_f16_kernel(const __half* __restrict_
             const float w = __shfl_sync(0xffffffffu, y, i);
             if (w == 0.0f) continue;
             const __half* vr = Vb + (size_t)(b0 + i) * kv_row;
-            for (int t = 0; t < dpl; ++t) acc[t] = fmaf(h2f(vr[lane + 32 * t]), w, acc[t]);
+            for (int t = 0; t < dpl; ++t)
+                if (lane + 32 * t < hda) acc[t] = fmaf(h2f(vr[lane + 32 * t]), w, acc[t]);
         }
         run_sum = __fadd_rn(run_sum, bsum);
     }
-    if (run_sum > 0.0f) {
-        const float inv = __fdiv_rn(1.0f, run_sum);
-        for (int t = 0; t < dpl; ++t) o[lane + 32 * t] = f2h(__fmul_rn(acc[t], inv));
-    } else {
-        for (int t = 0; t < dpl; ++t) o[lane + 32 * t] = __float2half_rn(0.0f);
+    const float inv = run_sum > 0.0f ? __fdiv_rn(1.0f, run_sum) : 0.0f;
+    for (int t = 0; t < dpl; ++t) {
+        const int d = lane + 32 * t;
+        if (d < D) o[d] = (run_sum > 0.0f && d < hda) ? f2h(__fmul_rn(acc[t], inv)) : __float2half_rn(0.0f);
     }
 }
 
@@ -247,24 +254,8 @@ __global__ void __launch_bounds__(128) attn_hybrid_kernel(
 // Thread (i = t/8, j = t%8) forms lane j of key i's 8-lane dot product; threads t < D own
 // output dim t. Raw INT8 K/V of the next blocks stream into shared memory with cp.async
 // (three buffers) while the current block is computed.
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// The online-softmax recurrence of the reference only chains the per-block (max, sum)
-// pair and the per-dim accumulator; scores, block maxima, weights and block sums of a block
-// depend on that block alone. So a chunk of up to 256 keys is processed in phases:
-//   1. all scores in parallel (8-lane dot products in the reference lane order),
-//   2. per 32-key block (one warp each): max, weights expf(s - max), in-order block sum,
-//   3. per output dim (one thread each): walk the blocks in order applying the correction
-//      expf(run_max - block_max) and the in-order V FMAs — the same operation sequence, so
-//      the result is bit-identical, with only the V chain left sequential.
+// One CTA of 256 threads per (batch, q head, query) runs the reference-order core
+// (attention_core.cuh) over chunks of 256 keys.
 template <int D>
 __global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
     const __half* __restrict__ Q, const int8_t* __restrict__ Kc, const int8_t* __restrict__ Vc,
@@ -278,17 +269,10 @@ __global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
         cache_len = dstate[0];
         pos_off = dstate[1];
     }
-    constexpr int CH = 256;  // keys per chunk (8 blocks of 32)
+    constexpr int CH = 256;
     extern __shared__ __align__(16) uint8_t smem[];
-    int8_t* kraw = reinterpret_cast<int8_t*>(smem);   // [CH][D]
-    int8_t* vraw = kraw + CH * D;                       // [CH][D]
-    float* qs = reinterpret_cast<float*>(vraw + CH * D);  // [D]
-    float* ksc = qs + D;                                // [CH][2]
-    float* vsc = ksc + CH * 2;                          // [CH][2]
-    float* sc = vsc + CH * 2;                           // [CH] scores, then weights
-    float* bmx = sc + CH;                               // [8]
-    float* bsm = bmx + 8;                               // [8]
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float* qs = reinterpret_cast<float*>(smem + attn_core_smem<D, CH>());
+    const int t = threadIdx.x;
     const long long item = blockIdx.x;
     const int qp = (int)(item % S);
     const int h = (int)((item / S) % Hq);
@@ -296,111 +280,37 @@ __global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
     const int kvh = h / (Hq / Hkv);
     const int nqg = (D + qgs - 1) / qgs;
     const size_t kv_row = (size_t)Hkv * D;
-    const int8_t* Kcb = Kc + b * kc_bstride + (size_t)kvh * D;
-    const int8_t* Vcb = Vc + b * kc_bstride + (size_t)kvh * D;
-    const float* ksb = ks + b * sc_bstride + (size_t)kvh * nqg;
-    const float* vsb = vs + b * sc_bstride + (size_t)kvh * nqg;
-    const __half* Knb = Kn + (size_t)b * new_len * kv_row + (size_t)kvh * D;
-    const __half* Vnb = Vn + (size_t)b * new_len * kv_row + (size_t)kvh * D;
     const __half* q16 = Q + (((size_t)b * S + qp) * Hq + h) * D;
     for (int d = t; d < D; d += 256) qs[d] = h2f(q16[d]);
 
+    AttnCoreArgs c;
+    c.qs = qs;
+    c.Kc = Kc + b * kc_bstride + (size_t)kvh * D;
+    c.Vc = Vc + b * kc_bstride + (size_t)kvh * D;
+    c.ks = ks + b * sc_bstride + (size_t)kvh * nqg;
+    c.vs = vs + b * sc_bstride + (size_t)kvh * nqg;
+    c.Kn = Kn + (size_t)b * new_len * kv_row + (size_t)kvh * D;
+    c.Vn = Vn + (size_t)b * new_len * kv_row + (size_t)kvh * D;
+    c.kv_row = (long long)kv_row;
+    c.sc_row = (long long)Hkv * nqg;
+    c.kn_row = (long long)kv_row;
+    c.cache_len = cache_len;
+    c.new_len = new_len;
+    c.qgs = qgs;
     const long long kv_seq_len = (long long)cache_len + new_len;
-    const long long aq = pos_off + qp;
-    const long long kv_end = causal ? min(kv_seq_len, aq + 1) : kv_seq_len;
-    float acc = 0.0f, run_max = -INFINITY, run_sum = 0.0f;
-
-    for (long long c0 = 0; c0 < kv_end; c0 += CH) {
-        const int n = (int)min((long long)CH, kv_end - c0);
-        const int ncached = (int)max(0LL, min((long long)n, (long long)cache_len - c0));
-        // stage the cached INT8 rows and scales of this chunk
-        for (int c = t; c < ncached * (D / 16); c += 256) {
-            const int i = c / (D / 16), off = (c % (D / 16)) * 16;
-            const size_t src = (size_t)(c0 + i) * kv_row + off;
-            cp_async16(kraw + i * D + off, Kcb + src);
-            cp_async16(vraw + i * D + off, Vcb + src);
-        }
-        for (int c = t; c < ncached * nqg; c += 256) {
-            const int i = c / nqg, g = c % nqg;
-            cp_async4(ksc + i * 2 + g, ksb + (size_t)(c0 + i) * Hkv * nqg + g);
-            cp_async4(vsc + i * 2 + g, vsb + (size_t)(c0 + i) * Hkv * nqg + g);
-        }
-        cp_async_commit();
-        cp_async_wait<0>();
-        __syncthreads();
-        // phase 1: scores (thread = lane kj of key ki's 8-lane dot product)
-        const int kj = t & 7;
-        for (int r = 0; r < CH / 32; ++r) {
-            const int i = (t >> 3) + 32 * r;
-            float a = 0.0f;
-            if (i < n) {
-                if (i < ncached) {
-                    const int8_t* kr = kraw + i * D;
-#pragma unroll
-                    for (int d = kj; d < D; d += 8) a = fmaf(qs[d], __fmul_rn((float)kr[d], ksc[i * 2 + d / qgs]), a);
-                } else {
-                    const __half* kr = Knb + (size_t)(c0 + i - cache_len) * kv_row;
-#pragma unroll
-                    for (int d = kj; d < D; d += 8) a = fmaf(qs[d], h2f(kr[d]), a);
-                }
-            }
-            const int base = lane & ~7;
-            float p[8];
-#pragma unroll
-            for (int m = 0; m < 8; ++m) p[m] = __shfl_sync(0xffffffffu, a, base + m);
-            float s = __fmul_rn(fold8(p), scale);
-            if (i >= n || (causal && c0 + i > aq)) s = -INFINITY;
-            if (kj == 0 && i < CH) sc[i] = s;
-        }
-        __syncthreads();
-        // phase 2: warp w owns block w of the chunk
-        const int nb = (n + 31) / 32;
-        if (warp < nb) {
-            const int i = warp * 32 + lane;
-            const int bs = min(32, n - warp * 32);
-            const float s = lane < bs ? sc[i] : -INFINITY;
-            const float m = warp_max(s);
-            const float w = (lane < bs && s != -INFINITY) ? expf_cr(__fsub_rn(s, m)) : 0.0f;
-            if (lane < bs) sc[i] = w;
-            float sum = 0.0f;
-            for (int l = 0; l < bs; ++l) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, w, l));
-            if (lane == 0) {
-                bmx[warp] = m;
-                bsm[warp] = sum;
-            }
-        }
-        __syncthreads();
-        // phase 3: the reference's sequential recurrence, one output dim per thread
-        for (int blk = 0; blk < nb; ++blk) {
-            const float m = bmx[blk];
-            if (m > -INFINITY) {
-                const float corr = expf_cr(__fsub_rn(run_max, m));
-                run_sum = __fmul_rn(run_sum, corr);
-                acc = __fmul_rn(acc, corr);
-                run_max = m;
-            }
-            if (t < D) {
-                const int i0 = blk * 32, i1 = min(n, i0 + 32);
-                for (int i = i0; i < i1; ++i) {
-                    const float w = sc[i];
-                    if (w == 0.0f) continue;
-                    float v;
-                    if (i < ncached) v = __fmul_rn((float)vraw[i * D + t], vsc[i * 2 + t / qgs]);
-                    else v = h2f(Vnb[(size_t)(c0 + i - cache_len) * kv_row + t]);
-                    acc = fmaf(v, w, acc);
-                }
-            }
-            run_sum = __fadd_rn(run_sum, bsm[blk]);
-        }
-        __syncthreads();
-    }
-    __half* o = O + (((size_t)b * S + qp) * Hq + h) * D;
-    if (t < D) o[t] = run_sum > 0.0f ? f2h(__fmul_rn(acc, __fdiv_rn(1.0f, run_sum))) : __float2half_rn(0.0f);
+    c.aq = pos_off + qp;
+    c.kv_end = causal ? min(kv_seq_len, c.aq + 1) : kv_seq_len;
+    c.causal = causal;
+    c.scale = scale;
+    c.prestaged = 0;
+    __syncthreads();
+    const __half r = attn_exact_core<D, 256, CH>(c, smem, SyncBlock{});
+    if (t < D) O[(((size_t)b * S + qp) * Hq + h) * D + t] = r;
 }
 
 template <int D>
 static size_t exact_smem() {
-    return (size_t)2 * 256 * D + (size_t)(D + 256 * 2 * 2 + 256 + 16) * 4;
+    return (size_t)attn_core_smem<D, 256>() + (size_t)D * 4;
 }
 
 int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks,

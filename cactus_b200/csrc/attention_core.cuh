@@ -1,0 +1,220 @@
+// Reference-order attention of one (query, head) against an INT8 cache plus FP16 new keys —
+// the arithmetic of cactus_attention_hybrid_int8_fp16 (kernel_attention.cpp:257-482):
+// 32-key blocks from key 0, scores as 8-lane dot products folded by a fixed tree, online
+// softmax whose running max is replaced by each block's max, exp() correctly rounded
+// (expf_cr) and the V accumulation per dim in key order.
+//
+// The recurrence only chains the per-block (max, sum) pair and the per-dim accumulator;
+// scores, block maxima, weights and block sums of a block depend on that block alone. So a
+// chunk of CH keys is processed in phases:
+//   1. all scores in parallel (8-lane dot products in the reference lane order),
+//   2. per 32-key block (one warp each): max, weights expf(s - max), in-order block sum,
+//   3. per output dim (one thread each): walk the blocks in order applying the correction
+//      expf(run_max - block_max) and the in-order V FMAs — the same operation sequence, so
+//      the result is bit-identical, with only the V chain left sequential.
+// Shared by the standalone attention kernel and the persistent decode kernel.
+#pragma once
+#include "common.cuh"
+
+namespace cb {
+
+__device__ __forceinline__ float fold8(const float* a) {
+    return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[1], a[5])),
+                     __fadd_rn(__fadd_rn(a[2], a[6]), __fadd_rn(a[3], a[7])));
+}
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// shared-memory footprint of attn_exact_core<D, CH> (a multiple of 16 bytes)
+template <int D, int CH>
+__host__ __device__ constexpr int attn_core_smem() {
+    return 2 * CH * D + (CH * 2 * 2 + CH + 3 * (CH / 32)) * 4;
+}
+
+struct SyncBlock {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+struct AttnCoreArgs {
+    const float* qs;      // [D] query as float (shared memory)
+    const int8_t* Kc;     // cache row 0 of this kv head: key i at Kc + i * kv_row
+    const int8_t* Vc;
+    const float* ks;      // scales of key i at ks + i * sc_row (nqg floats)
+    const float* vs;
+    const __half* Kn;     // new key j at Kn + j * kn_row (global or shared memory)
+    const __half* Vn;
+    long long kv_row, sc_row, kn_row;
+    int cache_len, new_len, qgs;
+    long long kv_end;     // keys [0, kv_end) are attended
+    long long aq;         // absolute query position (causal mask)
+    int causal;
+    float scale;
+    int prestaged;        // the caller already issued (and committed) chunk 0's cp.async copies
+};
+
+// Issues the cp.async copies of the cached INT8 rows and scales of chunk [c0, c0 + CH) and
+// commits them as one group (all NT threads call it).
+template <int D, int NT, int CH>
+__device__ __forceinline__ void attn_stage_chunk(const AttnCoreArgs& a, uint8_t* smem, long long c0) {
+    int8_t* kraw = reinterpret_cast<int8_t*>(smem);
+    int8_t* vraw = kraw + CH * D;
+    float* ksc = reinterpret_cast<float*>(vraw + CH * D);
+    float* vsc = ksc + CH * 2;
+    const int t = threadIdx.x;
+    const int nqg = (D + a.qgs - 1) / a.qgs;
+    const int n = (int)min((long long)CH, a.kv_end - c0);
+    const int ncached = (int)max(0LL, min((long long)n, (long long)a.cache_len - c0));
+    for (int c = t; c < ncached * (D / 16); c += NT) {
+        const int i = c / (D / 16), off = (c % (D / 16)) * 16;
+        const size_t src = (size_t)(c0 + i) * a.kv_row + off;
+        cp_async16(kraw + i * D + off, a.Kc + src);
+        cp_async16(vraw + i * D + off, a.Vc + src);
+    }
+    for (int c = t; c < ncached * nqg; c += NT) {
+        const int i = c / nqg, g = c % nqg;
+        cp_async4(ksc + i * 2 + g, a.ks + (size_t)(c0 + i) * a.sc_row + g);
+        cp_async4(vsc + i * 2 + g, a.vs + (size_t)(c0 + i) * a.sc_row + g);
+    }
+    cp_async_commit();
+}
+
+// Runs on NT threads that all call it; `bar` synchronises exactly those threads. Thread t < D
+// returns output dim t (fp16 bits); other threads return 0.
+template <int D, int NT, int CH, class Bar>
+__device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t* smem, Bar bar) {
+    static_assert(NT % 32 == 0 && NT >= D && NT >= 32 * (CH / 32), "thread count");
+    int8_t* kraw = reinterpret_cast<int8_t*>(smem);   // [CH][D]
+    int8_t* vraw = kraw + CH * D;                       // [CH][D]
+    float* ksc = reinterpret_cast<float*>(vraw + CH * D);  // [CH][2]
+    float* vsc = ksc + CH * 2;                          // [CH][2]
+    float* sc = vsc + CH * 2;                           // [CH] scores, then weights
+    float* bmx = sc + CH;                               // [CH/32] block maxima
+    float* bsm = bmx + CH / 32;                         // [CH/32] block sums
+    float* bcorr = bsm + CH / 32;                       // [CH/32] running-max corrections
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const float* qs = a.qs;
+    const int vg = t < D ? t / a.qgs : 0;  // V scale group of this thread's dim
+    float acc = 0.0f, run_max = -INFINITY, run_sum = 0.0f;
+    constexpr int KPR = NT / 8;                 // keys per scoring round
+
+    for (long long c0 = 0; c0 < a.kv_end; c0 += CH) {
+        const int n = (int)min((long long)CH, a.kv_end - c0);
+        const int ncached = (int)max(0LL, min((long long)n, (long long)a.cache_len - c0));
+        // stage the cached INT8 rows and scales of this chunk
+        if (!(c0 == 0 && a.prestaged)) attn_stage_chunk<D, NT, CH>(a, smem, c0);
+        cp_async_wait<0>();
+        bar();
+        // phase 1: scores (thread = lane kj of key ki's 8-lane dot product)
+        const int kj = t & 7;
+        const int rounds = (n + KPR - 1) / KPR;
+        for (int r = 0; r < rounds; ++r) {
+            const int i = (t >> 3) + KPR * r;
+            float acc8 = 0.0f;
+            if (i < n) {
+                if (i < ncached) {
+                    const int8_t* kr = kraw + i * D;
+                    // at most two scale groups per row (checked by the launchers)
+#pragma unroll
+                    for (int d = kj; d < D; d += 8)
+                        acc8 = fmaf(qs[d], __fmul_rn((float)kr[d], ksc[i * 2 + (d >= a.qgs ? 1 : 0)]), acc8);
+                } else {
+                    const __half* kr = a.Kn + (size_t)(c0 + i - a.cache_len) * a.kn_row;
+#pragma unroll
+                    for (int d = kj; d < D; d += 8) acc8 = fmaf(qs[d], h2f(kr[d]), acc8);
+                }
+            }
+            const int base = lane & ~7;
+            float p[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) p[m] = __shfl_sync(0xffffffffu, acc8, base + m);
+            float s = __fmul_rn(fold8(p), a.scale);
+            if (i >= n || (a.causal && c0 + i > a.aq)) s = -INFINITY;
+            if (kj == 0 && i < CH) sc[i] = s;
+        }
+        bar();
+        // phase 2: warp w owns block w of the chunk
+        const int nb = (n + 31) / 32;
+        if (warp < nb) {
+            const int i = warp * 32 + lane;
+            const int bs = min(32, n - warp * 32);
+            const float s = lane < bs ? sc[i] : -INFINITY;
+            const float m = warp_max(s);
+            const float w = (lane < bs && s != -INFINITY) ? expf_cr(__fsub_rn(s, m)) : 0.0f;
+            if (lane < bs) sc[i] = w;
+            float sum = 0.0f;
+#pragma unroll
+            for (int l = 0; l < 32; ++l) {
+                const float x = __shfl_sync(0xffffffffu, w, l);
+                if (l < bs) sum = __fadd_rn(sum, x);
+            }
+            if (lane == 0) {
+                bmx[warp] = m;
+                bsm[warp] = sum;
+            }
+        }
+        bar();
+        // the correction of block b, expf(running max before b - max of b), depends only on
+        // block maxima: computed for all blocks at once
+        if (t < nb) {
+            float pm = run_max;
+            for (int j = 0; j < t; ++j)
+                if (bmx[j] > -INFINITY) pm = bmx[j];
+            bcorr[t] = expf_cr(__fsub_rn(pm, bmx[t]));
+        }
+        bar();
+        // phase 3: the reference's sequential recurrence, one output dim per thread
+        for (int blk = 0; blk < nb; ++blk) {
+            const float m = bmx[blk];
+            if (m > -INFINITY) {
+                const float corr = bcorr[blk];
+                run_sum = __fmul_rn(run_sum, corr);
+                acc = __fmul_rn(acc, corr);
+                run_max = m;
+            }
+            if (t < D) {
+                // keys with weight 0 leave acc untouched (the reference skips them); a select
+                // keeps the loop branch-free so the loads of a block pipeline
+                const int i0 = blk * 32, i1 = min(n, i0 + 32);
+                const int ic = min(i1, max(i0, ncached));  // [i0, ic) cached, [ic, i1) new keys
+                const float* vs_t = vsc + vg;
+                if (ic - i0 == 32) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int i = i0 + j;
+                        const float w = sc[i];
+                        const float v = __fmul_rn((float)vraw[i * D + t], vs_t[i * 2]);
+                        const float nacc = fmaf(v, w, acc);
+                        acc = (w == 0.0f) ? acc : nacc;
+                    }
+                } else {
+                    for (int i = i0; i < ic; ++i) {
+                        const float w = sc[i];
+                        const float v = __fmul_rn((float)vraw[i * D + t], vs_t[i * 2]);
+                        const float nacc = fmaf(v, w, acc);
+                        acc = (w == 0.0f) ? acc : nacc;
+                    }
+                }
+                for (int i = ic; i < i1; ++i) {
+                    const float w = sc[i];
+                    const float v = h2f(a.Vn[(size_t)(c0 + i - a.cache_len) * a.kn_row + t]);
+                    const float nacc = fmaf(v, w, acc);
+                    acc = (w == 0.0f) ? acc : nacc;
+                }
+            }
+            run_sum = __fadd_rn(run_sum, bsm[blk]);
+        }
+        bar();
+    }
+    if (t >= D) return __float2half_rn(0.0f);
+    return run_sum > 0.0f ? f2h(__fmul_rn(acc, __fdiv_rn(1.0f, run_sum))) : __float2half_rn(0.0f);
+}
+
+}  // namespace cb

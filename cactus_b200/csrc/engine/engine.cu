@@ -306,8 +306,73 @@ void Engine::init(const std::string& folder, size_t context_size, size_t max_bat
                 throw std::runtime_error("rope table allocation failed");
         }
     }
+    setup_persistent();
     reset();
     ck(cudaStreamSynchronize(stream_), "init");
+}
+
+// Prepares the persistent decode step (decode_persistent.cu) when the model fits it: a
+// Qwen/Llama-style block with grouped INT8 projections and lm head sharing one group size.
+void Engine::setup_persistent() {
+    pplan_ = PPlan();
+    if (const char* m = std::getenv("CACTUS_B200_DECODE"))
+        if (std::string(m) == "graph") use_persistent_ = false;
+    auto no = [&](const char* why) { pplan_.ok = false; pplan_.why = why; };
+    if (cfg_.model_type == kGemma) return no("Gemma blocks use the per-op path");
+    const int G = lm_.G;
+    if (lm_.prec != kInt8) return no("lm head is not grouped INT8");
+    if (embed_.N < V_) return no("embedding table has fewer rows than the vocabulary");
+    for (const LayerW& lw : layers_)
+        for (const Mat* m : {&lw.qkv, &lw.o, &lw.gateup, &lw.down})
+            if (m->prec != kInt8 || m->G != G) return no("projections are not grouped INT8 with one group size");
+    std::vector<PLayer> pl(L_);
+    const size_t lstride = (size_t)max_batch_;
+    for (int l = 0; l < L_; ++l) {
+        const LayerW& lw = layers_[l];
+        PLayer& p = pl[l];
+        p.wqkv = static_cast<const int8_t*>(lw.qkv.data);
+        p.sqkv = lw.qkv.scales;
+        p.wo = static_cast<const int8_t*>(lw.o.data);
+        p.so = lw.o.scales;
+        p.wgu = static_cast<const int8_t*>(lw.gateup.data);
+        p.sgu = lw.gateup.scales;
+        p.wd = static_cast<const int8_t*>(lw.down.data);
+        p.sd = lw.down.scales;
+        p.in_norm = lw.in_norm;
+        p.post_norm = lw.post_attn_norm;
+        p.q_norm = lw.q_norm;
+        p.k_norm = lw.k_norm;
+        p.kc = kc_ + (size_t)l * lstride * cache_bstride_;
+        p.vc = vc_ + (size_t)l * lstride * cache_bstride_;
+        p.ks = ks_ + (size_t)l * lstride * scale_bstride_;
+        p.vs = vs_ + (size_t)l * lstride * scale_bstride_;
+        p.ct = ct_[l];
+        p.st = st_[l];
+    }
+    d_players_ = static_cast<PLayer*>(dmalloc(sizeof(PLayer) * L_, owned_));
+    ck(cudaMemcpy(d_players_, pl.data(), sizeof(PLayer) * L_, cudaMemcpyHostToDevice), "persistent layers");
+    psync_ = static_cast<PSync*>(dmalloc(sizeof(PSync), owned_));
+    PArgs& a = pargs_;
+    a = PArgs{};
+    a.layers = d_players_;
+    a.L = L_, a.H = H_, a.F = F_, a.Hq = Hq_, a.Hkv = Hkv_, a.D = D_, a.V = V_, a.G = G, a.QKVN = QKVN_;
+    a.lm_w = static_cast<const int8_t*>(lm_.data);
+    a.lm_s = lm_.scales;
+    a.out_norm = out_norm_;
+    a.emb = embed_.data;
+    a.emb_s = embed_.scales;
+    a.emb_prec = embed_.prec;
+    a.emb_G = embed_.G;
+    a.eps = cfg_.layer_norm_eps;
+    a.attn_scale = attention_scale_;
+    a.hidden = hidden_, a.qkv = qkv_, a.attn = attn_, a.gated = gated_, a.logits = logits_;
+    a.tok_in = tok_in_;
+    a.state = dstate_;
+    a.sync = psync_;
+    int sms = 0, optin = 0;
+    ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_), "sm count");
+    ck(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device_), "smem");
+    pplan_ = persistent_plan(a, sms, (size_t)optin);
 }
 
 bool Engine::is_global(int layer) const { return cfg_.model_type == kGemma && ((layer + 1) % 6) == 0; }
@@ -713,10 +778,21 @@ void Engine::generate(const uint32_t* prompts, int B, size_t P, size_t max_new, 
         ring_cap_ = ring_bytes;
     }
     push_state(0);
-    const bool can_graph = use_graph_ && cache_len_ > 0 && (window_ == 0 || cache_len_ + max_new <= window_) &&
-                           cache_len_ + max_new <= cap_;
+    const bool no_slide = cache_len_ > 0 && (window_ == 0 || cache_len_ + max_new <= window_) &&
+                          cache_len_ + max_new <= cap_;
+    const bool can_graph = use_graph_ && no_slide;
+    const bool can_persist = use_persistent_ && pplan_.ok && no_slide && B == 1;
     size_t step = 0;
-    if (!can_graph) {
+    if (can_persist) {
+        pargs_.ring = ring_;
+        ck(cudaMemsetAsync(psync_, 0, sizeof(PSync), stream_), "persistent sync");
+        for (; step < max_new; ++step) ck(launch_persistent_decode(pargs_, pplan_, stream_), "persistent decode");
+        cache_len_ += max_new;
+        total_len_ += max_new;
+        launches_ += (long long)max_new;
+        last_path_ = 2;
+    } else if (!can_graph) {
+        last_path_ = 0;
         for (; step < max_new; ++step) {
             // host-driven step: positions from the host mirror
             if (cache_len_ + 1 > cap_) throw std::runtime_error("KV cache capacity exceeded");
@@ -745,6 +821,7 @@ void Engine::generate(const uint32_t* prompts, int B, size_t P, size_t max_new, 
             graph_ring_ = ring_;
             graph_ring_stride_ = (int)max_new;
         }
+        last_path_ = 1;
         const long long before = launches_;
         for (; step < max_new; ++step) ck(cudaGraphLaunch(graph_exec_, stream_), "graph launch");
         replays = (long long)max_new;
@@ -758,6 +835,11 @@ void Engine::generate(const uint32_t* prompts, int B, size_t P, size_t max_new, 
                            stream_),
            "tokens out");
     ck(cudaStreamSynchronize(stream_), "generate");
+    if (last_path_ == 2) {
+        PSync ps;
+        ck(cudaMemcpy(&ps, psync_, sizeof(ps), cudaMemcpyDeviceToHost), "persistent sync");
+        if (ps.abort) throw std::runtime_error("persistent decode step gave up a bounded wait (device error recorded)");
+    }
     float a = 0, b = 0;
     ck(cudaEventElapsedTime(&a, ev_[0], ev_[1]), "elapsed");
     ck(cudaEventElapsedTime(&b, ev_[1], ev_[2]), "elapsed");
@@ -892,6 +974,13 @@ CB_API int cactus_engine_stats(cactus_engine_t engine, double* out8) {
     if (!engine || !out8) return CB_ERR_ARG;
     E(engine)->stats(out8);
     return CB_OK;
+}
+
+CB_API int cactus_engine_decode_path(cactus_engine_t engine, int mode) {
+    if (!engine) return -1;
+    if (mode == -1) E(engine)->use_persistent_ = true;
+    if (mode == 1) E(engine)->use_persistent_ = false;
+    return E(engine)->last_path_;
 }
 
 CB_API int cactus_engine_kv_state(cactus_engine_t engine, size_t* out2) {

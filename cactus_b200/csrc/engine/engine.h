@@ -9,6 +9,7 @@
 #include <string>
 #include <vector>
 
+#include "decode_persistent.h"
 #include "weights_io.h"
 
 namespace cb {
@@ -82,6 +83,9 @@ public:
 
     bool use_graph_ = true;
     bool use_pdl_ = true;
+    bool use_persistent_ = true;
+    int last_path_ = 0;  // 0 host loop, 1 CUDA graph, 2 persistent step
+    const std::string& persistent_reason() const { return pplan_.why; }
 
 private:
     Mat upload_mat(const std::vector<const HostTensor*>& parts, bool interleave_rows);
@@ -100,6 +104,7 @@ private:
     void run_forward_tokens(const uint32_t* tokens, int B, int S);
     void gather_last(int B, int S);
     void decode_step_device(int B, uint32_t* ring, int ring_stride, bool graph_mode);
+    void setup_persistent();
 
     Config cfg_;
     int device_ = 0;
@@ -136,6 +141,11 @@ private:
     long long launches_ = 0, last_launches_ = 0, last_graph_replays_ = 0;
     int graph_batch_ = 0, graph_ring_stride_ = 0;
     uint32_t* graph_ring_ = nullptr;
+    // persistent decode step
+    PArgs pargs_ = {};
+    PPlan pplan_;
+    PLayer* d_players_ = nullptr;
+    PSync* psync_ = nullptr;
 };
 
 }  // namespace eng

@@ -4,6 +4,7 @@
 #include "../common.cuh"
 #include "../gemv.cuh"
 #include "engine_kernels.h"
+#include "head_ops.cuh"
 
 namespace cb {
 namespace eng {
@@ -23,7 +24,7 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(QkvPostArgs a) {
     const long long item = (long long)blockIdx.x * 4 + warp;
     if (item >= (long long)a.rows * heads) return;
     const int row = (int)(item / heads), hi = (int)(item % heads);
-    const int D = a.D, half = D / 2;
+    const int D = a.D;
     const __half* src = a.qkv + (size_t)row * a.qkv_stride + (size_t)hi * D;
     if (hi >= a.Hq + a.Hkv) {  // value head: copy
         __half* dst = a.v_out + ((size_t)row * a.Hkv + (hi - a.Hq - a.Hkv)) * D;
@@ -31,43 +32,11 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(QkvPostArgs a) {
         return;
     }
     const bool is_q = hi < a.Hq;
-    const __half* nw = is_q ? a.q_norm : a.k_norm;
     for (int d = lane; d < D; d += 32) xs[d] = src[d];
     __syncwarp();
-    if (nw) {
-        const float ss = rms_sumsq_warp(xs, D);
-        const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps));
-        const float inv = __fdiv_rn(1.0f, rms);
-        const __half inv16 = __float2half_rn(inv);
-        const int vec_end = (D / 8) * 8;
-        __syncwarp();
-        for (int d = lane; d < D; d += 32) {
-            const __half v = xs[d];
-            xs[d] = d < vec_end ? __hmul(__hmul(v, inv16), nw[d])
-                                : __float2half_rn(__fmul_rn(__fmul_rn(h2f(v), inv), h2f(nw[d])));
-        }
-        __syncwarp();
-    }
     const long long pos = (a.dstate ? (long long)a.dstate[1] : a.pos_base) + (row % a.S);
     __half* dst = is_q ? a.q_out + ((size_t)row * a.Hq + hi) * D : a.k_out + ((size_t)row * a.Hkv + (hi - a.Hq)) * D;
-    if (a.ct == nullptr) {  // rope disabled (rope_theta <= 0)
-        for (int d = lane; d < D; d += 32) dst[d] = xs[d];
-        return;
-    }
-    const __half* c = a.ct + pos * half;
-    const __half* sn = a.st + pos * half;
-    const int vec_half = (half / 8) * 8;
-    for (int i = lane; i < half; i += 32) {
-        const __half x1 = xs[i], x2 = xs[i + half];
-        if (i < vec_half) {
-            dst[i] = __hfma(__hneg(x2), sn[i], __hmul(x1, c[i]));
-            dst[i + half] = __hfma(x1, sn[i], __hmul(x2, c[i]));
-        } else {
-            const float f1 = h2f(x1), f2 = h2f(x2), fc = h2f(c[i]), fs = h2f(sn[i]);
-            dst[i] = f2h(__fsub_rn(__fmul_rn(f1, fc), __fmul_rn(f2, fs)));
-            dst[i + half] = f2h(__fadd_rn(__fmul_rn(f2, fc), __fmul_rn(f1, fs)));
-        }
-    }
+    head_norm_rope_warp(xs, D, is_q ? a.q_norm : a.k_norm, a.eps, a.ct, a.st, pos, dst);
 }
 
 // ------------------------------------------------------------------ KV append
@@ -98,18 +67,7 @@ __global__ void kv_append_kernel(KvAppendArgs a) {
                       ((size_t)(dst0 + t) * a.Hkv + h) * a.D + g0;
         float* sdst = (which ? a.v_scales : a.k_scales) + (size_t)b * a.scale_bstride +
                       ((size_t)(dst0 + t) * a.Hkv + h) * ng + g;
-        float mx = 0.0f;
-        for (int k = lane; k < cnt; k += 32) mx = fmaxf(mx, fabsf(h2f(src[k])));
-        mx = warp_max(mx);
-        float scale = __fdiv_rn(mx, 127.0f);
-        if (scale < 1e-10f) scale = 1e-10f;
-        const float inv = __fdiv_rn(1.0f, scale);
-        const int vec = (cnt / 8) * 8;
-        for (int k = lane; k < cnt; k += 32) {
-            const float v = __fmul_rn(h2f(src[k]), inv);
-            dst[k] = (int8_t)sat8(k < vec ? cvt_rne_sat(v) : (int)roundf(v));
-        }
-        if (lane == 0) *sdst = scale;
+        kv_quant_group_warp(src, cnt, dst, sdst);
     }
 }
 

@@ -81,13 +81,25 @@ __host__ __device__ inline GemvLayout gemv_layout(int wf, int MT, int RPW, int S
 // 16 lane accumulators over 16-element tiles, an 8-element tail tile into lanes 0..7, the
 // fixed combine tree and a scalar tail. Runs on one warp; result broadcast to all lanes.
 __device__ __forceinline__ float rms_sumsq_warp(const __half* xs, int K) {
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, l16 = lane & 15;
     float acc = 0.0f;
-    int i = 0;
-    const int tile_end = K >= 16 ? K - 16 + 1 : 0;
-#pragma unroll 8
-    for (; i < tile_end; i += 16)
-        if (lane < 16) { float v = h2f(xs[i + lane]); acc = fmaf(v, v, acc); }
+    // lane l (< 16) accumulates elements l, l + 16, ... of the full 16-element tiles in
+    // order; loads are batched 8 tiles at a time so only the FMA chain is sequential (lanes
+    // 16..31 mirror lanes 0..15 and are ignored by the fold below)
+    const int ntiles = K / 16;
+    int tt = 0;
+    for (; tt + 8 <= ntiles; tt += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = h2f(xs[(tt + j) * 16 + l16]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(v[j], v[j], acc);
+    }
+    for (; tt < ntiles; ++tt) {
+        const float v = h2f(xs[tt * 16 + l16]);
+        acc = fmaf(v, v, acc);
+    }
+    int i = ntiles * 16;
     const int simd_end = K >= 8 ? K - 8 + 1 : 0;
     if (i < simd_end) {
         if (lane < 8) { float v = h2f(xs[i + lane]); acc = fmaf(v, v, acc); }

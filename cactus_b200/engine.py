@@ -78,6 +78,11 @@ class Engine:
         self._check(self._L.cactus_engine_last_logits(self.h, out.ctypes.data_as(C.c_void_p), self.vocab), "logits")
         return out
 
+    def decode_path(self, mode: int = 0) -> int:
+        """Decode path of the last generate (0 host loop, 1 CUDA graph, 2 persistent step);
+        mode -1 re-enables the persistent step, 1 disables it for later calls."""
+        return int(self._L.cactus_engine_decode_path(self.h, mode))
+
     def stats(self):
         out = np.zeros(8, np.float64)
         self._check(self._L.cactus_engine_stats(self.h, out.ctypes.data_as(C.c_void_p)), "stats")

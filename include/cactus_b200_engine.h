@@ -69,6 +69,12 @@ CB_API int cactus_engine_generate_batch_greedy(cactus_engine_t engine, const uin
  * nodes per replay, out[5] weight bytes in HBM, out[6] KV capacity, out[7] KV window */
 CB_API int cactus_engine_stats(cactus_engine_t engine, double* out8);
 
+/* decode path of the last generate call: 0 host-driven launches, 1 CUDA-graph replay of
+ * the per-op kernels, 2 persistent single-launch decode step (batch 1, non-Gemma models).
+ * `mode` selects the path for later calls: -1 automatic (persistent where it applies),
+ * 1 never use the persistent step. Returns the last path, or -1 for a null engine. */
+CB_API int cactus_engine_decode_path(cactus_engine_t engine, int mode);
+
 /* fp16 logits of the last decoded row of sequence 0 (for parity checks) */
 CB_API int cactus_engine_last_logits(cactus_engine_t engine, uint16_t* host_logits, size_t vocab);
 /* KV state of sequence 0: out[0] = current_seq_len, out[1] = total_seq_len (engine_cache.cpp:101-337) */

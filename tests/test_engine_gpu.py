@@ -107,6 +107,39 @@ def test_batched_sequences_are_independent(folders):
     eng.close()
 
 
+PERSISTENT_KINDS = {
+    "qwen": lambda: convert.tiny("qwen", layers=2),
+    "qwen_g128": lambda: convert.tiny("qwen", layers=2, group_size=128),
+    "qwen_d128": lambda: convert.tiny("qwen", layers=3, heads=4, kv_heads=1, head_dim=128, hidden=384, ffn=768,
+                                      vocab=2048),
+    "llama_int8": lambda: convert.tiny("smol", layers=2, theta=5e5),
+}
+
+
+@pytest.mark.parametrize("kind", list(PERSISTENT_KINDS))
+def test_persistent_decode_matches_graph_path_and_oracle(tmp_path_factory, kind):
+    """The single-launch persistent decode step and the per-op CUDA-graph path produce the
+    same tokens, bit-identical logits and KV-cache bytes, and both match the oracle."""
+    folder = convert.make_model(str(tmp_path_factory.mktemp("p_" + kind)), PERSISTENT_KINDS[kind](), seed=4,
+                                norm_std=0.1)
+    prompt = np.random.default_rng(9).integers(0, 1000, 40).tolist()
+    res = {}
+    for mode in (-1, 1):
+        eng = Engine(folder, context_size=512)
+        eng.decode_path(mode)
+        toks = eng.generate_greedy(prompt, 24).tolist()
+        res[mode] = (toks, eng.decode_path(), eng.last_logits(), eng.read_kv(1), eng.kv_state())
+        eng.close()
+    assert res[-1][1] == 2 and res[1][1] == 1
+    assert res[-1][0] == res[1][0]
+    assert np.array_equal(res[-1][2].view(np.uint16), res[1][2].view(np.uint16))
+    for a, b in zip(res[-1][3], res[1][3]):
+        assert np.array_equal(a, b)
+    assert res[-1][4] == res[1][4]
+    ref = OM.RefModel(folder, context_size=512)
+    assert res[-1][0] == ref.generate_greedy(prompt, 24)
+
+
 def test_engine_rejects_out_of_range_tokens(folders):
     eng = Engine(folders["qwen"], context_size=64)
     with pytest.raises(Exception, match="out of bounds"):
@@ -123,6 +156,7 @@ def test_qwen3_0_6b_greedy_32_tokens_identical(tmp_path_factory):
     prompt = np.random.default_rng(0).integers(0, arch.vocab_size, 128).tolist()
     eng = Engine(folder, context_size=512)
     got = eng.generate_greedy(prompt, 32).tolist()
+    assert eng.decode_path() == 2  # the persistent single-launch step
     ref = OM.RefModel(folder, context_size=512)
     exp = ref.generate_greedy(prompt, 32)
     assert got == exp
