@@ -364,6 +364,48 @@ CB_API int cactus_cuda_sample_f16(const uint16_t* logits, size_t rows, size_t vo
     return check_launch("sample_f16");
 }
 
+// ---- sampling without caller scratch: the filtered-logits buffer is a fixed file-scope
+// device array (one per device and per loaded copy of this library); nothing is allocated.
+namespace {
+constexpr size_t kStaticSampleVocab = 262144;  // largest vocabulary of the supported models
+__device__ __align__(256) uint16_t g_sample_scratch[kStaticSampleVocab];
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+}  // namespace
+
+CB_API int cactus_cuda_sample_f16_noalloc(const uint16_t* logits, size_t rows, size_t vocab, float temperature,
+                                          float top_p, size_t top_k, float uniform, const uint32_t* history,
+                                          size_t n_history, uint32_t* out_index, void* stream) {
+    if (rows == 0 || vocab == 0) return fail(CB_ERR_ARG, "sample_noalloc: empty logits");
+    if (vocab > kStaticSampleVocab)
+        return fail(CB_ERR_ARG, "sample_noalloc: vocab " + std::to_string(vocab) + " exceeds the static scratch of " +
+                                    std::to_string(kStaticSampleVocab) + " entries");
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return fail(CB_ERR_LAUNCH, "sample_noalloc: no usable current device");
+    }
+    void* scratch = nullptr;
+    {
+        // set-up on the first call per device: resolve the array's address once
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        if (!g_scratch_ptr[dev]) {
+            void* p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_sample_scratch);
+            if (e != cudaSuccess || !p) {
+                cudaGetLastError();
+                return fail(CB_ERR_LAUNCH, std::string("sample_noalloc: cudaGetSymbolAddress failed: ") +
+                                               cudaGetErrorString(e));
+            }
+            g_scratch_ptr[dev] = p;
+        }
+        scratch = g_scratch_ptr[dev];
+    }
+    return cactus_cuda_sample_f16(logits, rows, vocab, temperature, top_p, top_k, uniform, history, n_history,
+                                  static_cast<uint16_t*>(scratch), out_index, stream);
+}
+
 CB_API int cactus_cuda_entropy_f16(const uint16_t* logits, size_t rows, size_t vocab, float* out, void* stream) {
     if (rows == 0 || vocab == 0) return fail(CB_ERR_ARG, "entropy: empty logits");
     cb::launch_entropy(H(logits) + (rows - 1) * vocab, (int)vocab, out, S(stream));

@@ -137,6 +137,18 @@ CB_API int cactus_cuda_argmax_f16(const uint16_t* logits, size_t rows, size_t vo
 CB_API int cactus_cuda_sample_f16(const uint16_t* logits, size_t rows, size_t vocab, float temperature, float top_p,
                                   size_t top_k, float uniform, const uint32_t* history, size_t n_history,
                                   uint16_t* work, uint32_t* out_index, void* stream);
+/* ---- cactus_cuda_sample_f16 without the `work` argument; no counterpart in the reference.
+ *      For callers that must not allocate device memory (code running inside CUDA stream
+ *      capture, or under an allocator they do not control). The scratch is a fixed array
+ *      inside this library holding up to 262144 fp16 entries per device; larger vocabularies
+ *      are rejected with CB_ERR_ARG. Nothing in it needs to start at zero (every entry used is
+ *      written before it is read). The first call on each device resolves the array's address
+ *      (cudaGetSymbolAddress); make it before any stream capture. Calls that overlap in time
+ *      on one device (different streams or host threads) share the array and race: serialise
+ *      them. Results equal cactus_cuda_sample_f16's. */
+CB_API int cactus_cuda_sample_f16_noalloc(const uint16_t* logits, size_t rows, size_t vocab, float temperature,
+                                          float top_p, size_t top_k, float uniform, const uint32_t* history,
+                                          size_t n_history, uint32_t* out_index, void* stream);
 /* ---- normalised entropy of softmax(logits[rows-1]) (engine_model.cpp:255-290), fp32 out */
 CB_API int cactus_cuda_entropy_f16(const uint16_t* logits, size_t rows, size_t vocab, float* out, void* stream);
 
