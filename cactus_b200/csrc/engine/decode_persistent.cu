@@ -32,15 +32,15 @@ namespace eng {
 
 namespace {
 
-constexpr int kPT = 512;       // threads per block
-constexpr int kPCW = 15;       // consumer warps
+constexpr int kPCW = 11;       // consumer warps
 constexpr int kPC = kPCW * 32; // consumer threads
+constexpr int kPT = kPC + 32;  // + one producer warp; 384 threads leave ~170 registers a thread
 constexpr int kACH = 256;      // attention keys per staged chunk
 constexpr int kStaticSmem = 1024;
 
 enum : int { kEpiStore = 0, kEpiResid = 1, kEpiGlu = 2, kEpiLm = 3 };
 
-__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 480;" ::: "memory"); }
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(kPC) : "memory"); }
 struct SyncConsumers {
     __device__ __forceinline__ void operator()() const { cbar(); }
 };
@@ -95,6 +95,7 @@ __device__ void producer(const PArgs& a, uint8_t* ring, uint64_t* full, uint64_t
     unsigned k = 0;
     bool ok = true;
     const int J = 4 * a.L + 1;
+    const uint64_t stream_policy = l2_policy_evict_first();
     for (int j = 0; j < J && ok; ++j) {
         const JobW jw = job_w(a, j);
         int r0, r1;
@@ -110,8 +111,8 @@ __device__ void producer(const PArgs& a, uint8_t* ring, uint64_t* full, uint64_t
             const unsigned wb = (unsigned)(rows * jw.K), sbytes = (unsigned)(rows * ng * 2);
             uint8_t* dst = ring + (size_t)s * sb;
             mbar_arrive_expect_tx(&full[s], wb + sbytes);
-            tma_load_1d(dst, jw.w + (size_t)r * jw.K, wb, &full[s]);
-            tma_load_1d(dst + a.slot_w, jw.s + (size_t)r * ng, sbytes, &full[s]);
+            tma_load_1d_hint(dst, jw.w + (size_t)r * jw.K, wb, &full[s], stream_policy);
+            tma_load_1d_hint(dst + a.slot_w, jw.s + (size_t)r * ng, sbytes, &full[s], stream_policy);
             ++k;
         }
     }
@@ -126,6 +127,7 @@ __device__ void producer(const PArgs& a, uint8_t* ring, uint64_t* full, uint64_t
 struct Cs {  // consumer shared memory
     int8_t* act;
     __half* xs;
+    __half* xsT;  // lane-major copy for the RMS chain
     int* gsm;
     float* gsf;
     __half* ob;
@@ -135,58 +137,96 @@ struct Cs {  // consumer shared memory
     unsigned long long* best;  // [16]
 };
 
-constexpr int kMaxPerThread = 8;  // activation elements per consumer thread (K <= 3840)
-constexpr int kMaxPass = 8;       // 512-element passes of one GEMV row (K <= 4096)
+constexpr int kMaxCpg = 8;  // 16-byte chunks per quantisation group (G <= 128)
 
-// Stages K fp16 activations written by other blocks (L2 loads) into xs; when `src` is null
-// the caller has filled xs already. The optional RMSNorm weights of the following prologue
-// are fetched into registers first, so their latency overlaps the staging.
-__device__ __forceinline__ void load_vec(__half* xs, const __half* src, int K, const __half* norm,
-                                         __half (&nw)[kMaxPerThread]) {
-    if (norm) {
+// Shared-memory work in these phases is latency-bound (one warp at a time on a dependent
+// chain), so activations move as 16-byte chunks: one thread per 8 consecutive elements.
+
+// Stages K fp16 activations written by other blocks (L2 loads) into xs (src == null: xs is
+// filled already). With `transposed`, also writes xsT, the lane-major copy the RMS chain
+// reads with 16-byte loads: element k at (k % 16) * (K/16 + 8) + k / 16.
+__device__ __forceinline__ void load_vec(const Cs& m, const __half* src, int K, bool transposed) {
+    const int4* s4 = reinterpret_cast<const int4*>(src);
+    int4* d4 = reinterpret_cast<int4*>(m.xs);
+    const int TS = K / 16 + 8;
+    for (int i = threadIdx.x; i < K / 8; i += kPC) {
+        const int4 v = src ? __ldcg(s4 + i) : d4[i];
+        if (src) d4[i] = v;
+        if (transposed) {
+            const __half* h = reinterpret_cast<const __half*>(&v);
 #pragma unroll
-        for (int j = 0; j < kMaxPerThread; ++j) {
-            const int k = threadIdx.x + j * kPC;
-            if (k < K) nw[j] = norm[k];
+            for (int j = 0; j < 8; ++j) m.xsT[(8 * (i & 1) + j) * TS + (i >> 1)] = h[j];
         }
-    }
-    if (src) {
-        const int4* s4 = reinterpret_cast<const int4*>(src);
-        int4* d4 = reinterpret_cast<int4*>(xs);
-        for (int i = threadIdx.x; i < K / 8; i += kPC) d4[i] = __ldcg(s4 + i);
     }
     cbar();
 }
 
-// xs holds K fp16 activations; optional RMSNorm with weights `nw` (registers, from
-// load_vec), then the activation quantisation (gemv.cuh prologues, same arithmetic) into
-// act / *as.
-__device__ void prologue(const Cs& m, int K, bool norm, const __half (&nw)[kMaxPerThread], float eps) {
+// RMSNorm sum of squares (rms_sumsq_warp's order, K % 16 == 0) from the lane-major copy:
+// lane l < 16 walks its 16-element tiles in order with one 16-byte load per 8 tiles.
+__device__ __forceinline__ float rms_sumsq_lanemajor(const __half* xsT, int K) {
+    const int lane = threadIdx.x & 31, l16 = lane & 15, T = K / 16;
+    const int4* p = reinterpret_cast<const int4*>(xsT + l16 * (T + 8));
+    float acc = 0.0f;
+    for (int c = 0; c < T / 8; ++c) {
+        const int4 v = p[c];
+        const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float f = h2f(h[j]);
+            acc = fmaf(f, f, acc);
+        }
+    }
+    for (int t = (T / 8) * 8; t < T; ++t) {
+        const float f = h2f(xsT[l16 * (T + 8) + t]);
+        acc = fmaf(f, f, acc);
+    }
+    const float a4 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 4);
+    const float a8 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 8);
+    const float a12 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 12);
+    const float a0 = __shfl_sync(0xffffffffu, acc, lane & 3);
+    const float t4 = __fadd_rn(__fadd_rn(__fadd_rn(a0, a4), a8), a12);
+    const float t0 = __shfl_sync(0xffffffffu, t4, 0), t1 = __shfl_sync(0xffffffffu, t4, 1);
+    const float t2 = __shfl_sync(0xffffffffu, t4, 2), t3 = __shfl_sync(0xffffffffu, t4, 3);
+    return __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
+}
+
+// xs holds K fp16 activations (K % 8 == 0; K % 16 == 0 with a norm); optional RMSNorm with
+// weights `normw` (the load_vec call must have passed transposed = true), then the
+// activation quantisation (gemv.cuh prologues, same arithmetic) into act / *as.
+__device__ __forceinline__ void prologue(const Cs& m, int K, const __half* normw, float eps) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int vec_end = (K / 8) * 8;
+    const int nch = K / 8;
+    int4* x4 = reinterpret_cast<int4*>(m.xs);
     float mx = 0.0f;
-    if (norm) {
+    if (normw) {
         if (warp == 0) {
-            const float ss = rms_sumsq_warp(m.xs, K);
+            const float ss = rms_sumsq_lanemajor(m.xsT, K);
             if (lane == 0) m.red[32] = ss;
         }
         cbar();
         const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(m.red[32], (float)K), eps));
         const float inv_rms = __fdiv_rn(1.0f, rms);
         const __half inv16 = __float2half_rn(inv_rms);
+        const int4* w4 = reinterpret_cast<const int4*>(normw);
+        for (int i = tid; i < nch; i += kPC) {
+            int4 v = x4[i];
+            const int4 w = __ldg(w4 + i);
+            __half* h = reinterpret_cast<__half*>(&v);
+            const __half* hw = reinterpret_cast<const __half*>(&w);
 #pragma unroll
-        for (int j = 0; j < kMaxPerThread; ++j) {
-            const int k = tid + j * kPC;
-            if (k < K) {
-                __half v = m.xs[k];
-                v = (k < vec_end) ? __hmul(__hmul(v, inv16), nw[j])
-                                  : __float2half_rn(__fmul_rn(__fmul_rn(h2f(v), inv_rms), h2f(nw[j])));
-                m.xs[k] = v;
-                mx = fmaxf(mx, fabsf(h2f(v)));
+            for (int j = 0; j < 8; ++j) {
+                h[j] = __hmul(__hmul(h[j], inv16), hw[j]);
+                mx = fmaxf(mx, fabsf(h2f(h[j])));
             }
+            x4[i] = v;
         }
     } else {
-        for (int k = tid; k < K; k += kPC) mx = fmaxf(mx, fabsf(h2f(m.xs[k])));
+        for (int i = tid; i < nch; i += kPC) {
+            int4 v = x4[i];
+            const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(h2f(h[j])));
+        }
     }
     mx = warp_max(mx);
     if (lane == 0) m.red[warp] = mx;
@@ -196,7 +236,16 @@ __device__ void prologue(const Cs& m, int K, bool norm, const __half (&nw)[kMaxP
     float scale = __fdiv_rn(mxa, 127.0f);
     if (scale < 1e-10f) scale = 1e-10f;
     const float inv = __fdiv_rn(1.0f, scale);
-    for (int k = tid; k < K; k += kPC) m.act[k] = quant_act(h2f(m.xs[k]), inv, k < vec_end);
+    int2* a2 = reinterpret_cast<int2*>(m.act);
+    for (int i = tid; i < nch; i += kPC) {
+        int4 v = x4[i];
+        const __half* h = reinterpret_cast<const __half*>(&v);
+        int2 q;
+        int8_t* qb = reinterpret_cast<int8_t*>(&q);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) qb[j] = quant_act(h2f(h[j]), inv, true);
+        a2[i] = q;
+    }
     if (tid == 0) *m.as = scale;
     cbar();
 }
@@ -210,21 +259,23 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
 
 // One projection of the block's rows: grouped INT8 GEMV (exact int32 group sums, fp32 FMA
 // chain over the groups in order, times the activation scale -> fp16) + epilogue.
-__device__ bool gemv_job(const PArgs& a, int j, int epi, const Cs& m, uint8_t* ring, uint64_t* full,
+__device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const Cs& m, uint8_t* ring, uint64_t* full,
                          uint64_t* empty, unsigned& kslot, __half* out, unsigned long long& best) {
     const int tid = threadIdx.x;
     const JobW jw = job_w(a, j);
     int r0, r1;
     rows_of(jw.N, blockIdx.x, gridDim.x, r0, r1);
-    const int K = jw.K, ng = K / a.G, spr = rows_per_slot(a.slot_w, K), cpg = a.G / 16, gst = ng + 1;
-    const int cpg_log2 = __ffs(cpg) - 1, chunks = K / 16, npass = (chunks + 31) / 32;
-    const int lane = tid & 31, warp = tid >> 5;
-    int4 areg[kMaxPass];  // this lane's activation chunks, one per pass
+    // group sums / scales of row r at [r * gst, r * gst + ng): gst keeps rows 16-byte aligned
+    // and puts consecutive rows in different banks for the 16-byte loads of the chain
+    const int K = jw.K, ng = K / a.G, spr = rows_per_slot(a.slot_w, K), cpg = a.G / 16, gst = ((ng + 3) & ~3) + 4;
+    // thread -> (row, group): the group is fixed for the whole job (so its activation chunks
+    // stay in registers) and a round covers rpr rows
+    const int rpr = kPC / ng, g = tid % ng, r_first = tid / ng;
+    const bool tactive = r_first < rpr;
+    int4 ar[kMaxCpg];
 #pragma unroll
-    for (int p = 0; p < kMaxPass; ++p) {
-        const int c = p * 32 + lane;
-        areg[p] = (p < npass && c < chunks) ? *reinterpret_cast<const int4*>(m.act + c * 16) : make_int4(0, 0, 0, 0);
-    }
+    for (int c = 0; c < kMaxCpg; ++c)
+        ar[c] = (tactive && c < cpg) ? *reinterpret_cast<const int4*>(m.act + g * a.G + c * 16) : make_int4(0, 0, 0, 0);
     const float as = *m.as;
     const int NS = a.nslots, sb = a.slot_w + a.slot_s;
     for (int r = r0; r < r1; r += spr, ++kslot) {
@@ -240,43 +291,39 @@ __device__ bool gemv_job(const PArgs& a, int j, int epi, const Cs& m, uint8_t* r
         mbar_wait_bounded(&full[s], par);  // completed already: makes the copy visible to this thread
         const uint8_t* wsl = ring + (size_t)s * sb;
         const uint16_t* ssl = reinterpret_cast<const uint16_t*>(wsl + a.slot_w);
-        // warp per row, lane per 16-byte chunk (chunk lane + 32p of pass p); the activation
-        // chunks live in registers for the whole job; lanes of a group fold by xor shuffles
-        for (int rr = warp; rr < rows; rr += kPCW) {
-            const uint8_t* wrow = wsl + (size_t)rr * K;
-            int part[kMaxPass];
+        // exact int32 sum of each (row, group): cpg 16-byte chunks, 4 dp4a each
+        if (tactive) {
+            for (int rr = r_first; rr < rows; rr += rpr) {
+                const int4* wp = reinterpret_cast<const int4*>(wsl + (size_t)rr * K + g * a.G);
+                int acc = 0;
 #pragma unroll
-            for (int p = 0; p < kMaxPass; ++p) {
-                part[p] = 0;
-                if (p < npass && (p * 32 + lane) < chunks) {
-                    const int4 wv = *reinterpret_cast<const int4*>(wrow + (p * 32 + lane) * 16);
-                    int acc = dp4a_ss(areg[p].x, wv.x, 0);
-                    acc = dp4a_ss(areg[p].y, wv.y, acc);
-                    acc = dp4a_ss(areg[p].z, wv.z, acc);
-                    part[p] = dp4a_ss(areg[p].w, wv.w, acc);
-                }
-            }
-#pragma unroll
-            for (int p = 0; p < kMaxPass; ++p) {
-                if (p < npass) {
-                    int acc = part[p];
-                    for (int o = 1; o < cpg; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                    const int c = p * 32 + lane;
-                    if (c < chunks && (lane & (cpg - 1)) == 0) {
-                        const int g = c >> cpg_log2;
-                        m.gsm[rr * gst + g] = acc;
-                        m.gsf[rr * gst + g] = h2f_bits(ssl[rr * ng + g]);
+                for (int c = 0; c < kMaxCpg; ++c) {
+                    if (c < cpg) {
+                        const int4 wv = wp[c];
+                        acc = dp4a_ss(ar[c].x, wv.x, acc);
+                        acc = dp4a_ss(ar[c].y, wv.y, acc);
+                        acc = dp4a_ss(ar[c].z, wv.z, acc);
+                        acc = dp4a_ss(ar[c].w, wv.w, acc);
                     }
                 }
+                m.gsm[rr * gst + g] = acc;
+                m.gsf[rr * gst + g] = h2f_bits(ssl[rr * ng + g]);
             }
         }
         cbar();
         if (tid < rows) {
-            const int* gp = m.gsm + tid * gst;
-            const float* fp = m.gsf + tid * gst;
+            const int4* gp = reinterpret_cast<const int4*>(m.gsm + tid * gst);
+            const float4* fp = reinterpret_cast<const float4*>(m.gsf + tid * gst);
             float run = 0.0f;
-#pragma unroll 8
-            for (int g = 0; g < ng; ++g) run = fmaf((float)gp[g], fp[g], run);
+            for (int c = 0; c < ng / 4; ++c) {
+                const int4 gv = gp[c];
+                const float4 fv = fp[c];
+                run = fmaf((float)gv.x, fv.x, run);
+                run = fmaf((float)gv.y, fv.y, run);
+                run = fmaf((float)gv.z, fv.z, run);
+                run = fmaf((float)gv.w, fv.w, run);
+            }
+            for (int g = ng & ~3; g < ng; ++g) run = fmaf((float)m.gsm[tid * gst + g], m.gsf[tid * gst + g], run);
             const __half v = f2h(__fmul_rn(run, as));
             const int n = r + tid;
             if (epi == kEpiStore) {
@@ -300,7 +347,7 @@ __device__ bool gemv_job(const PArgs& a, int j, int epi, const Cs& m, uint8_t* r
 }
 
 // grid-wide barrier over the consumer warps of all blocks
-__device__ bool grid_sync(const PArgs& a, unsigned& nbar, int* flag) {
+__device__ __forceinline__ bool grid_sync(const PArgs& a, unsigned& nbar, int* flag) {
     cbar();
     ++nbar;
     if (threadIdx.x == 0) {
@@ -397,7 +444,7 @@ __device__ __forceinline__ void attention_prefetch(const PArgs& a, int l, int h,
 }
 
 template <int D>
-__device__ void attention_head(const PArgs& a, int l, int h, uint8_t* work, int cache_len, int total_len) {
+__device__ __forceinline__ void attention_head(const PArgs& a, int l, int h, uint8_t* work, int cache_len, int total_len) {
     const int tid = threadIdx.x, warp = tid >> 5;
     const int grp = a.Hq / a.Hkv, kvh = h / grp;
     const int nqg = (D + 127) / 128;
@@ -434,7 +481,7 @@ __device__ void attention_head(const PArgs& a, int l, int h, uint8_t* work, int 
 
 // embedding row of `tok` (compute_embedding_node semantics, as embed_kernel) into xs; the
 // block also stores its slice of the hidden state
-__device__ void embed_row(const PArgs& a, uint32_t tok, __half* xs) {
+__device__ __forceinline__ void embed_row(const PArgs& a, uint32_t tok, __half* xs) {
     const int H = a.H;
     const int k0 = (int)(((long long)H * blockIdx.x) / gridDim.x), k1 = (int)(((long long)H * (blockIdx.x + 1)) / gridDim.x);
     for (int k = threadIdx.x; k < H; k += kPC) {
@@ -491,6 +538,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     m.gsm = reinterpret_cast<int*>(work + a128(a.kmax) + a128(2 * a.kmax));
     m.gsf = reinterpret_cast<float*>(m.gsm + a.gsm_ints);
     m.ob = reinterpret_cast<__half*>(m.gsf + a.gsm_ints);
+    m.xsT = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(m.ob) + a128(a.max_rows * 2));
     m.red = s_red;
     m.as = &s_as;
     m.flag = &s_flag;
@@ -502,32 +550,31 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     const bool attn_block = (int)blockIdx.x < a.Hq;
     unsigned kslot = 0, nbar = 0;
     unsigned long long best = 0ull;
-    __half nw[kMaxPerThread];
     embed_row(a, tok, m.xs);
     for (int l = 0; l < a.L; ++l) {
         const PLayer& ly = a.layers[l];
         if (attn_block) attention_prefetch<D>(a, l, blockIdx.x, awork, cache_len, total_len);
-        load_vec(m.xs, l > 0 ? a.hidden : nullptr, a.H, ly.in_norm, nw);
-        prologue(m, a.H, true, nw, a.eps);
+        load_vec(m, l > 0 ? a.hidden : nullptr, a.H, true);
+        prologue(m, a.H, ly.in_norm, a.eps);
         if (!gemv_job(a, 4 * l, kEpiStore, m, ring, full, empty, kslot, a.qkv, best)) return;
         if (!grid_sync(a, nbar, m.flag)) return;
         if (attn_block) attention_head<D>(a, l, blockIdx.x, awork, cache_len, total_len);
         if (!grid_sync(a, nbar, m.flag)) return;
-        load_vec(m.xs, a.attn, a.Hq * D, nullptr, nw);
-        prologue(m, a.Hq * D, false, nw, a.eps);
+        load_vec(m, a.attn, a.Hq * D, false);
+        prologue(m, a.Hq * D, nullptr, a.eps);
         if (!gemv_job(a, 4 * l + 1, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
         if (!grid_sync(a, nbar, m.flag)) return;
-        load_vec(m.xs, a.hidden, a.H, ly.post_norm, nw);
-        prologue(m, a.H, true, nw, a.eps);
+        load_vec(m, a.hidden, a.H, true);
+        prologue(m, a.H, ly.post_norm, a.eps);
         if (!gemv_job(a, 4 * l + 2, kEpiGlu, m, ring, full, empty, kslot, a.gated, best)) return;
         if (!grid_sync(a, nbar, m.flag)) return;
-        load_vec(m.xs, a.gated, a.F, nullptr, nw);
-        prologue(m, a.F, false, nw, a.eps);
+        load_vec(m, a.gated, a.F, false);
+        prologue(m, a.F, nullptr, a.eps);
         if (!gemv_job(a, 4 * l + 3, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
         if (!grid_sync(a, nbar, m.flag)) return;
     }
-    load_vec(m.xs, a.hidden, a.H, a.out_norm, nw);
-    prologue(m, a.H, true, nw, a.eps);
+    load_vec(m, a.hidden, a.H, true);
+    prologue(m, a.H, a.out_norm, a.eps);
     if (!gemv_job(a, 4 * a.L, kEpiLm, m, ring, full, empty, kslot, a.logits, best)) return;
     // block first-max, then the last block to finish picks the token
     for (int o = 16; o > 0; o >>= 1) {
@@ -592,11 +639,13 @@ PPlan persistent_plan(PArgs& a, int num_sms, size_t smem_optin) {
     a.slot_s = a128(a.slot_w / a.G * 2);
     a.max_rows = a.slot_w / kmin;
     if (a.max_rows > kPC) return no("hidden sizes too small for the slot size");
-    a.gsm_ints = a.slot_w / a.G + a.max_rows + 32;
-    if (a.H > kMaxPerThread * kPC) return no("hidden size above the per-thread RMSNorm limit");
-    if (kmax > kMaxPass * 512) return no("projection width above 4096");
+    a.gsm_ints = (a.slot_w / a.G + 8 * a.max_rows + 32 + 3) / 4 * 4;
+    if (a.G > 16 * kMaxCpg) return no("group size above 128");
+    if (kmax / a.G > kPC) return no("more groups per row than consumer threads");
     if (a.G & (a.G - 1)) return no("group size must be a power of two");
-    const int gemv_work = a128(kmax) + a128(2 * kmax) + 2 * a.gsm_ints * 4 + a.max_rows * 2 + 16;
+    if (a.H % 16) return no("hidden size must be a multiple of 16");
+    const int gemv_work = a128(kmax) + a128(2 * kmax) + 2 * a.gsm_ints * 4 + a128(a.max_rows * 2) +
+                          a128(16 * (a.H / 16 + 8) * 2);
     const int attn_work = a.D == 64 ? attn_work_bytes<64>() : attn_work_bytes<128>();
     a.attn_off = a128(gemv_work);
     a.work_bytes = a.attn_off + a128(attn_work);

@@ -117,6 +117,49 @@ __device__ __forceinline__ float rms_sumsq_warp(const __half* xs, int K) {
     return ss;
 }
 
+// Shared-memory load helpers: explicit ld.shared (the compiler cannot always prove a pointer
+// is shared inside large kernels and then emits slower generic loads).
+__device__ __forceinline__ float lds_h2f(uint32_t saddr) {
+    unsigned short u;
+    asm volatile("ld.shared.b16 %0, [%1];" : "=h"(u) : "r"(saddr));
+    return __half2float(__ushort_as_half(u));
+}
+
+// rms_sumsq_warp on a shared-memory address (same operation order).
+__device__ __forceinline__ float rms_sumsq_warp_sh(uint32_t xs, int K) {
+    const int lane = threadIdx.x & 31, l16 = lane & 15;
+    float acc = 0.0f;
+    const int ntiles = K / 16;
+    int tt = 0;
+    for (; tt + 8 <= ntiles; tt += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = lds_h2f(xs + 2u * ((tt + j) * 16 + l16));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(v[j], v[j], acc);
+    }
+    for (; tt < ntiles; ++tt) {
+        const float v = lds_h2f(xs + 2u * (tt * 16 + l16));
+        acc = fmaf(v, v, acc);
+    }
+    int i = ntiles * 16;
+    const int simd_end = K >= 8 ? K - 8 + 1 : 0;
+    if (i < simd_end) {
+        if (lane < 8) { float v = lds_h2f(xs + 2u * (i + lane)); acc = fmaf(v, v, acc); }
+        i += 8;
+    }
+    float a4 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 4);
+    float a8 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 8);
+    float a12 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 12);
+    float a0 = __shfl_sync(0xffffffffu, acc, lane & 3);
+    float t = __fadd_rn(__fadd_rn(__fadd_rn(a0, a4), a8), a12);
+    float t0 = __shfl_sync(0xffffffffu, t, 0), t1 = __shfl_sync(0xffffffffu, t, 1);
+    float t2 = __shfl_sync(0xffffffffu, t, 2), t3 = __shfl_sync(0xffffffffu, t, 3);
+    float ss = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
+    for (; i < K; ++i) { float v = lds_h2f(xs + 2u * i); ss = fmaf(v, v, ss); }
+    return ss;
+}
+
 // Quantize one fp16 value with the reference's activation rule; `vec` selects the
 // NEON vector path (RNE after clamping) versus the scalar tail (round half away).
 __device__ __forceinline__ int8_t quant_act(float v, float inv, bool vec) {
