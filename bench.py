@@ -51,6 +51,9 @@ def parse():
                     help="only time the GEMV kernel class (one token's projections) and print its roofline")
     ap.add_argument("--layers", type=int, default=0, help="--kernel-only: number of layers (default: all)")
     ap.add_argument("--decode", type=int, default=DECODE, help="decode tokens per request (profiling runs use fewer)")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 5],
+                    help="2 (default): the headline decode line; 1 / 5: the matmul / attention sweeps, one "
+                         "JSON line per shape")
     return ap.parse_args()
 
 
@@ -244,6 +247,113 @@ def run_reference(args):
     return 0
 
 
+def _peaks():
+    f = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    pk = json.load(open(f)) if os.path.exists(f) else {}
+    return float(pk.get("hbm_gbs", 6650.0)), float(pk.get("bf16_tflops", 1590.0)), \
+        "measured" if "hbm_gbs" in pk else "fallback"
+
+
+def run_config1(args):
+    """Config 1: graph-level grouped INT8 matmul, W [3072, 1024] (row = output column), A fp16
+    [M, 1024], M in {1, 128}, G in {32, 128}, through cactus_cuda_linear_int8 (activation
+    quantisation fused). 64 weight copies (> L2) rotate inside one CUDA graph."""
+    import torch
+    import cactus_b200 as cb
+    L = cb.lib()
+    torch.cuda.set_device(0)
+    hbm, _, src = _peaks()
+    N, K, copies = 3072, 1024, 64
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    for G in (32, 128):
+        ws = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g) for _ in range(copies)]
+        ss = [(torch.rand((N, K // G), device="cuda", generator=g) * 1e-3).half() for _ in range(copies)]
+        for M in (1, 128):
+            x = torch.randn((M, K), device="cuda", generator=g).half()
+            y = torch.empty((M, N), device="cuda", dtype=torch.half)
+            stream = torch.cuda.Stream()
+            with torch.cuda.stream(stream):
+                def launch():
+                    for w, sc in zip(ws, ss):
+                        cb.check(L.cactus_cuda_linear_int8(x.data_ptr(), w.data_ptr(), sc.data_ptr(), y.data_ptr(), M,
+                                                           K, N, G, stream.cuda_stream), "linear_int8")
+                for _ in range(3):
+                    launch()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    launch()
+                for _ in range(3):
+                    graph.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = max(args.steps, 5)
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+                e1.synchronize()
+            ms = e0.elapsed_time(e1) / reps / copies
+            nbytes = N * K + N * (K // G) * 2 + M * K * 2 + M * N * 2
+            flops = 2.0 * M * N * K
+            del graph
+            print(json.dumps({"config": 1, "workload": f"int8 linear M={M} K={K} N={N} G={G}", "us_per_matmul": ms * 1e3,
+                              "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (ms / 1e3) / 1e9,
+                              "frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / hbm, "tflops": flops / (ms / 1e3) / 1e12,
+                              "peak_source": src, "l2": f"{copies} rotating weight copies > L2"}), flush=True)
+    return 0
+
+
+def run_config5(args):
+    """Config 5 (decode half): INT8-cache attention, 16 q / 8 kv heads, D=128, one query per
+    sequence, L in {512, 4096, 32768} cached keys, B in {1, 8, 64}, through
+    cactus_cuda_attention_hybrid_int8_fp16. L2 is flushed (a 256 MB write) before each timed call."""
+    import torch
+    import cactus_b200 as cb
+    L = cb.lib()
+    torch.cuda.set_device(0)
+    hbm, _, src = _peaks()
+    Hq, Hkv, D = 16, 8, 128
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    for Lc in (512, 4096, 32768):
+        for B in (1, 8, 64):
+            kc = torch.randint(-127, 128, (B, Lc, Hkv, D), dtype=torch.int8, device="cuda", generator=g)
+            vc = torch.randint(-127, 128, (B, Lc, Hkv, D), dtype=torch.int8, device="cuda", generator=g)
+            ks = torch.rand((Lc, Hkv, 1), device="cuda", generator=g) * 0.02
+            vs = torch.rand((Lc, Hkv, 1), device="cuda", generator=g) * 0.02
+            q = torch.randn((B, 1, Hq, D), device="cuda", generator=g).half()
+            kn = torch.randn((B, 1, Hkv, D), device="cuda", generator=g).half()
+            vn = torch.randn((B, 1, Hkv, D), device="cuda", generator=g).half()
+            o = torch.empty_like(q)
+            st = torch.cuda.current_stream().cuda_stream
+
+            def call():
+                cb.check(L.cactus_cuda_attention_hybrid_int8_fp16(
+                    q.data_ptr(), kc.data_ptr(), vc.data_ptr(), ks.data_ptr(), vs.data_ptr(), kn.data_ptr(),
+                    vn.data_ptr(), o.data_ptr(), B, 1, Lc, 1, Hq, Hkv, D, 1.0 / D ** 0.5, Lc, 1, 128, st),
+                    "attention_hybrid")
+            for _ in range(3):
+                call()
+            times = []
+            for _ in range(max(args.steps, 3)):
+                flush.fill_(1)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                call()
+                e1.record()
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1))
+            ms = sorted(times)[len(times) // 2]
+            nbytes = B * 2112 * Lc + B * Hq * D * 4 + B * Hkv * D * 4
+            print(json.dumps({"config": 5, "workload": f"decode attention INT8 cache L={Lc} B={B} (16/8 heads, D=128)",
+                              "us": ms * 1e3, "algorithmic_bytes": nbytes,
+                              "achieved_gbs": nbytes / (ms / 1e3) / 1e9, "frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / hbm,
+                              "peak_source": src, "l2": "flushed before each call"}), flush=True)
+            del kc, vc
+    return 0
+
+
 def run_kernel_only(args):
     import torch
     from cactus_b200 import convert
@@ -267,6 +377,10 @@ def main():
         return run_reference(args)
     if args.kernel_only:
         return run_kernel_only(args)
+    if args.config == 1:
+        return run_config1(args)
+    if args.config == 5:
+        return run_config5(args)
     import torch
     rank, local_rank, world = dist_env()
     torch.cuda.set_device(local_rank)

@@ -142,13 +142,17 @@ constexpr int kMaxCpg = 8;  // 16-byte chunks per quantisation group (G <= 128)
 // Shared-memory work in these phases is latency-bound (one warp at a time on a dependent
 // chain), so activations move as 16-byte chunks: one thread per 8 consecutive elements.
 
+// Row stride (halves) of the lane-major copy of a K-element vector: K/16 rounded up to 8,
+// plus 8 of padding (rows stay 16-byte aligned and fall into different banks).
+__host__ __device__ constexpr int lanemajor_stride(int K) { return ((K / 16 + 7) & ~7) + 8; }
+
 // Stages K fp16 activations written by other blocks (L2 loads) into xs (src == null: xs is
 // filled already). With `transposed`, also writes xsT, the lane-major copy the RMS chain
-// reads with 16-byte loads: element k at (k % 16) * (K/16 + 8) + k / 16.
+// reads with 16-byte loads: element k at (k % 16) * lanemajor_stride(K) + k / 16.
 __device__ __forceinline__ void load_vec(const Cs& m, const __half* src, int K, bool transposed) {
     const int4* s4 = reinterpret_cast<const int4*>(src);
     int4* d4 = reinterpret_cast<int4*>(m.xs);
-    const int TS = K / 16 + 8;
+    const int TS = lanemajor_stride(K);
     for (int i = threadIdx.x; i < K / 8; i += kPC) {
         const int4 v = src ? __ldcg(s4 + i) : d4[i];
         if (src) d4[i] = v;
@@ -164,8 +168,8 @@ __device__ __forceinline__ void load_vec(const Cs& m, const __half* src, int K, 
 // RMSNorm sum of squares (rms_sumsq_warp's order, K % 16 == 0) from the lane-major copy:
 // lane l < 16 walks its 16-element tiles in order with one 16-byte load per 8 tiles.
 __device__ __forceinline__ float rms_sumsq_lanemajor(const __half* xsT, int K) {
-    const int lane = threadIdx.x & 31, l16 = lane & 15, T = K / 16;
-    const int4* p = reinterpret_cast<const int4*>(xsT + l16 * (T + 8));
+    const int lane = threadIdx.x & 31, l16 = lane & 15, T = K / 16, TS = lanemajor_stride(K);
+    const int4* p = reinterpret_cast<const int4*>(xsT + l16 * TS);
     float acc = 0.0f;
     for (int c = 0; c < T / 8; ++c) {
         const int4 v = p[c];
@@ -177,7 +181,7 @@ __device__ __forceinline__ float rms_sumsq_lanemajor(const __half* xsT, int K) {
         }
     }
     for (int t = (T / 8) * 8; t < T; ++t) {
-        const float f = h2f(xsT[l16 * (T + 8) + t]);
+        const float f = h2f(xsT[l16 * TS + t]);
         acc = fmaf(f, f, acc);
     }
     const float a4 = __shfl_sync(0xffffffffu, acc, (lane & 3) + 4);
@@ -645,7 +649,7 @@ PPlan persistent_plan(PArgs& a, int num_sms, size_t smem_optin) {
     if (a.G & (a.G - 1)) return no("group size must be a power of two");
     if (a.H % 16) return no("hidden size must be a multiple of 16");
     const int gemv_work = a128(kmax) + a128(2 * kmax) + 2 * a.gsm_ints * 4 + a128(a.max_rows * 2) +
-                          a128(16 * (a.H / 16 + 8) * 2);
+                          a128(16 * lanemajor_stride(a.H) * 2);
     const int attn_work = a.D == 64 ? attn_work_bytes<64>() : attn_work_bytes<128>();
     a.attn_off = a128(gemv_work);
     a.work_bytes = a.attn_off + a128(attn_work);

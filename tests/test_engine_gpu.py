@@ -113,6 +113,8 @@ PERSISTENT_KINDS = {
     "qwen_d128": lambda: convert.tiny("qwen", layers=3, heads=4, kv_heads=1, head_dim=128, hidden=384, ffn=768,
                                       vocab=2048),
     "llama_int8": lambda: convert.tiny("smol", layers=2, theta=5e5),
+    "smol_576": lambda: convert.tiny("smol", layers=2, hidden=576, heads=9, kv_heads=3, head_dim=64, ffn=1536,
+                                     theta=1e5),
 }
 
 
