@@ -135,8 +135,58 @@ static int gemv_or_chunks(cb::GemvCall c, size_t M, size_t K, size_t N, size_t G
     return check_launch(name);
 }
 
+// ---- M >= 16 rows: the tensor-core GEMM (gemm.cu), same result bits as the GEMV
+// Grow-only per-device scratch for the quantised activations of linear_* calls (old buffers
+// stay allocated so kernels already queued on other streams keep valid pointers).
+namespace {
+std::mutex g_gemm_mu;
+std::map<int, std::pair<void*, size_t>> g_gemm_scratch;
+void* gemm_scratch(size_t bytes) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_gemm_mu);
+    auto& e = g_gemm_scratch[dev];
+    if (e.second < bytes) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        e = {p, bytes};
+    }
+    return e.first;
+}
+
+// the GEMM stages rows with 16-byte copies and the scales with 8-byte copies
+bool use_gemm(size_t M, size_t K, size_t N, size_t G, int int4, const void* A, const void* B, const void* Bs) {
+    return M >= (size_t)cb::kGemmMinRows && M <= kIntMax && K <= kIntMax && N <= kIntMax && G <= kIntMax &&
+           cb::gemm_check((int)M, (int)K, (int)N, (int)G, int4) == nullptr && (!A || aligned16(A)) &&
+           aligned16(B) && (reinterpret_cast<uintptr_t>(Bs) & 7) == 0;
+}
+
+int gemm_preq(const int8_t* A, const float* As, const void* B, const uint16_t* Bs, uint16_t* C, size_t M, size_t K,
+              size_t N, size_t G, int int4, const char* name, cudaStream_t st) {
+    if (cb::launch_gemm(A, As, B, H(Bs), H(C), nullptr, (int)M, (int)K, (int)N, (int)G, int4, cb::kEpiStore, st) != 0)
+        return fail(CB_ERR_LAUNCH, std::string(name) + ": gemm launch failed");
+    return check_launch(name);
+}
+
+int gemm_linear(const uint16_t* X, const void* B, const uint16_t* Bs, uint16_t* C, size_t M, size_t K, size_t N,
+                size_t G, int int4, const char* name, cudaStream_t st) {
+    const size_t qbytes = (M * K + 255) / 256 * 256;
+    uint8_t* scratch = static_cast<uint8_t*>(gemm_scratch(qbytes + M * 4));
+    if (!scratch) return fail(CB_ERR_LAUNCH, std::string(name) + ": scratch allocation failed");
+    int8_t* aq = reinterpret_cast<int8_t*>(scratch);
+    float* as = reinterpret_cast<float*>(scratch + qbytes);
+    cb::launch_quantize_act(H(X), aq, as, (int)M, (int)K, st);
+    return gemm_preq(aq, as, B, Bs, C, M, K, N, G, int4, name, st);
+}
+}  // namespace
+
 CB_API int cactus_cuda_matmul_int8(const int8_t* A, const float* A_scales, const int8_t* B, const uint16_t* B_scales,
                                    uint16_t* C, size_t M, size_t K, size_t N, size_t group_size, void* stream) {
+    if (use_gemm(M, K, N, group_size, 0, A, B, B_scales))
+        return gemm_preq(A, A_scales, B, B_scales, C, M, K, N, group_size, 0, "matmul_int8", S(stream));
     cb::GemvCall c = {};
     c.int4 = 0;
     c.pro = cb::kProPreq;
@@ -152,6 +202,8 @@ CB_API int cactus_cuda_matmul_int8(const int8_t* A, const float* A_scales, const
 CB_API int cactus_cuda_matmul_int4(const int8_t* A, const float* A_scales, const uint8_t* B_packed,
                                    const uint16_t* B_scales, uint16_t* C, size_t M, size_t K, size_t N,
                                    size_t group_size, void* stream) {
+    if (use_gemm(M, K, N, group_size, 1, A, B_packed, B_scales))
+        return gemm_preq(A, A_scales, B_packed, B_scales, C, M, K, N, group_size, 1, "matmul_int4", S(stream));
     cb::GemvCall c = {};
     c.int4 = 1;
     c.pro = cb::kProPreq;
@@ -166,6 +218,8 @@ CB_API int cactus_cuda_matmul_int4(const int8_t* A, const float* A_scales, const
 
 CB_API int cactus_cuda_linear_int8(const uint16_t* X, const int8_t* B, const uint16_t* B_scales, uint16_t* C, size_t M,
                                    size_t K, size_t N, size_t group_size, void* stream) {
+    if (use_gemm(M, K, N, group_size, 0, nullptr, B, B_scales))
+        return gemm_linear(X, B, B_scales, C, M, K, N, group_size, 0, "linear_int8", S(stream));
     cb::GemvCall c = {};
     c.int4 = 0;
     c.pro = cb::kProQuant;
@@ -179,6 +233,8 @@ CB_API int cactus_cuda_linear_int8(const uint16_t* X, const int8_t* B, const uin
 
 CB_API int cactus_cuda_linear_int4(const uint16_t* X, const uint8_t* B_packed, const uint16_t* B_scales, uint16_t* C,
                                    size_t M, size_t K, size_t N, size_t group_size, void* stream) {
+    if (use_gemm(M, K, N, group_size, 1, nullptr, B_packed, B_scales))
+        return gemm_linear(X, B_packed, B_scales, C, M, K, N, group_size, 1, "linear_int4", S(stream));
     cb::GemvCall c = {};
     c.int4 = 1;
     c.pro = cb::kProQuant;

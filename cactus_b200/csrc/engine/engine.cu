@@ -289,6 +289,10 @@ void Engine::init(const std::string& folder, size_t context_size, size_t max_bat
     xnorm_ = static_cast<__half*>(dmalloc((size_t)max_batch_ * H_ * 2, owned_));
     logits_ = static_cast<__half*>(dmalloc((size_t)max_batch_ * V_ * 2, owned_));
     ids_ = static_cast<uint32_t*>(dmalloc(R * 4, owned_));
+    const size_t kmax = (size_t)std::max({H_, Hq_ * D_, F_});
+    gm_xn_ = static_cast<__half*>(dmalloc(R * H_ * 2, owned_));
+    gm_aq_ = static_cast<int8_t*>(dmalloc(R * kmax, owned_));
+    gm_as_ = static_cast<float*>(dmalloc(R * 4, owned_));
     tok_in_ = static_cast<uint32_t*>(dmalloc((size_t)max_batch_ * 4, owned_));
     dstate_ = static_cast<int*>(dmalloc(4 * sizeof(int), owned_));
     hist_dev_ = static_cast<uint32_t*>(dmalloc(128 * 4, owned_));
@@ -402,6 +406,22 @@ void Engine::push_state(int step) {
 // ------------------------------------------------------------------ GEMV helper (chunks of 8 rows)
 void Engine::gemv(const Mat& w, int pro, int epi, const __half* x, const __half* norm, __half* out,
                   const __half* resid, int M) {
+    if (M >= kGemmMinRows && w.prec != kFp16 && gemm_check(M, w.K, w.N, w.G, w.prec == kInt4) == nullptr) {
+        // prefill: normalise / quantise the rows once, then the tensor-core GEMM (same bits)
+        const __half* xq = x;
+        if (pro == kProRmsNormQuant) {
+            launch_rms_norm(x, norm, gm_xn_, M, w.K, cfg_.layer_norm_eps, stream_);
+            xq = gm_xn_;
+            ++launches_;
+        }
+        launch_quantize_act(xq, gm_aq_, gm_as_, M, w.K, stream_);
+        if (launch_gemm(gm_aq_, gm_as_, w.data, w.scales, out, resid, M, w.K, w.N, w.G, w.prec == kInt4 ? 1 : 0, epi,
+                        stream_) != 0)
+            throw std::runtime_error("gemm launch failed");
+        ck(cudaGetLastError(), "gemm launch");
+        launches_ += 2;
+        return;
+    }
     for (int m0 = 0; m0 < M; m0 += 8) {
         GemvCall c = {};
         c.int4 = w.prec == kInt4 ? 1 : 0;

@@ -129,6 +129,9 @@ private:
     __half *hidden_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *kall_ = nullptr, *vall_ = nullptr;
     __half *attn_ = nullptr, *tmp_o_ = nullptr, *gated_ = nullptr, *last_ = nullptr, *xnorm_ = nullptr;
     __half* logits_ = nullptr;
+    __half* gm_xn_ = nullptr;  // prefill GEMM staging: normalised rows, int8 rows, row scales
+    int8_t* gm_aq_ = nullptr;
+    float* gm_as_ = nullptr;
     uint32_t *ids_ = nullptr, *tok_in_ = nullptr, *ring_ = nullptr, *hist_dev_ = nullptr;
     __half* sample_work_ = nullptr;
     float* f32_scratch_ = nullptr;

@@ -30,6 +30,12 @@ int launch_gemv(const GemvCall& c, cudaStream_t st);
 void gemv_prepare();  // set kernel attributes of all variants (call before graph capture)
 const char* gemv_check(const GemvCall& c);  // nullptr when the shape is supported
 
+// ---- grouped INT8 / INT4 GEMM for M >= 16 on the tensor cores (gemm.cu); A pre-quantised
+const char* gemm_check(int M, int K, int N, int G, int int4);  // nullptr when supported
+int launch_gemm(const int8_t* aq, const float* as, const void* w, const __half* ws, __half* out, const __half* resid,
+                int M, int K, int N, int G, int int4, int epi, cudaStream_t st);
+constexpr int kGemmMinRows = 16;  // below this the GEMV is faster
+
 // ---- misc (misc.cu)
 int launch_quantize_act(const __half* x, int8_t* q, float* s, int M, int K, cudaStream_t st);
 int launch_rms_norm(const __half* x, const __half* w, __half* y, int rows, int dims, float eps, cudaStream_t st);

@@ -56,7 +56,11 @@ def _weights(rng, N, K, G, int4=False):
 @pytest.mark.parametrize("int4", [False, True])
 @pytest.mark.parametrize("M,K,N,G", [(1, 1024, 3072, 32), (1, 1024, 3072, 128), (2, 2048, 1000, 64),
                                       (5, 640, 520, 32), (8, 1024, 4096, 128), (13, 3072, 1024, 32),
-                                      (1, 8192, 264, 32)])
+                                      (1, 8192, 264, 32),
+                                      # M >= 16: the tensor-core GEMM path
+                                      (16, 1024, 3072, 32), (127, 2048, 1024, 32), (64, 3072, 1024, 128),
+                                      (33, 640, 512, 32), (200, 1024, 4096, 64), (17, 576, 960, 32),
+                                      (130, 1024, 96, 128)])
 def test_matmul_prequantized_bit_exact(L, ref, int4, M, K, N, G):
     if int4 and G % 32:
         pytest.skip("INT4 groups are multiples of 32")
