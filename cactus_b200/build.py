@@ -4,6 +4,13 @@ One nvcc invocation compiles every ``csrc/**/*.cu`` and ``csrc/**/*.cpp``:
 ``-gencode arch=compute_100a,code=sm_100a -O3 -lineinfo --fmad=false``. ``--fmad=false``
 keeps a*b+c unfused unless a kernel asks for fmaf() explicitly, which is how the
 kernels reproduce the reference's rounding points.
+
+Sources are relocatable device code (``-rdc=true``, linked with one device-link step) except
+WHOLE_PROGRAM: tcgen05.mma kernels built as relocatable code read their shared-memory
+operands from the wrong place (measured on B200 with nvcc 12.9: the same kernel and
+descriptors give exact products as whole-program code and scrambled ones under -rdc), so
+those files are compiled whole-program and reach the rest of the library through host
+calls and kernel arguments only.
 """
 from __future__ import annotations
 
@@ -17,6 +24,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libcactus_b200.so")
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
+WHOLE_PROGRAM = ("gemm_tc.cu",)
 
 
 def sources():
@@ -58,7 +66,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     if verbose:
         common += ["-Xptxas", "-v"]
     stamp = os.path.join(objdir, "flags.txt")
-    flags_str = " ".join(common) + " rdc"
+    flags_str = " ".join(common) + " rdc wp=" + ",".join(WHOLE_PROGRAM)
     if not os.path.exists(stamp) or open(stamp).read() != flags_str:
         force = True
     objs, procs = [], []
@@ -69,7 +77,8 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
         objs.append(obj)
         if not force and os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(f) for f in _deps()):
             continue
-        cmd = [nvcc(), *common, "-rdc=true", "-c", src, "-o", obj]
+        rdc = [] if os.path.basename(src) in WHOLE_PROGRAM else ["-rdc=true"]
+        cmd = [nvcc(), *common, *rdc, "-c", src, "-o", obj]
         procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)))
         while len([p for _, p in procs if p.poll() is None]) >= jobs:
             procs[0][1].wait() if procs[0][1].poll() is None else None

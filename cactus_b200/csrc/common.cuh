@@ -25,9 +25,14 @@ enum DevError : unsigned {
     kDevTmaTimeout = 1,
     kDevFlagTimeout = 2,
 };
+#ifdef __CUDACC_RDC__
 extern __device__ unsigned g_dev_error;
 
 __device__ __forceinline__ void report_dev_error(unsigned code) { atomicCAS(&g_dev_error, 0u, code); }
+#endif
+// Address of g_dev_error for kernels compiled as whole-program code (no extern device
+// symbols there): they take it as a kernel argument.
+unsigned* dev_error_ptr();
 
 // ---------------------------------------------------------------- fp16 helpers
 __device__ __forceinline__ float h2f(__half h) { return __half2float(h); }

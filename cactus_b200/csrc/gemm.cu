@@ -14,6 +14,9 @@
 // expanded to int8 when the B fragment is built: low nibble = even k) and the chunk's fp16
 // group scales. Epilogues: store, residual add (fp16), SiLU / GELU gate x up on interleaved
 // gate/up columns.
+#include <cstdlib>
+#include <string>
+
 #include "attention_core.cuh"
 #include "common.cuh"
 #include "ops.h"
@@ -207,6 +210,15 @@ int launch_one(const GemmArgs& g, cudaStream_t st) {
 }
 }  // namespace
 
+// CACTUS_B200_GEMM=mma keeps every M >= 16 product on the mma.sync kernel (comparison runs)
+bool gemm_tc_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("CACTUS_B200_GEMM");
+        return !(e && std::string(e) == "mma");
+    }();
+    return on;
+}
+
 const char* gemm_check(int M, int K, int N, int G, int int4) {
     if (M < 1 || K < 1 || N < 1) return "empty matrix";
     if (N % kBN) return "N must be a multiple of 32";
@@ -215,9 +227,15 @@ const char* gemm_check(int M, int K, int N, int G, int int4) {
     return nullptr;
 }
 
+bool gemm_tc_ok(int M, int K, int N, int G, int int4);
+int launch_gemm_tc(const int8_t* aq, const float* as, const int8_t* w, const __half* ws, __half* out,
+                   const __half* resid, int M, int K, int N, int G, int epi, cudaStream_t st);
+
 int launch_gemm(const int8_t* aq, const float* as, const void* w, const __half* ws, __half* out, const __half* resid,
                 int M, int K, int N, int G, int int4, int epi, cudaStream_t st) {
     if (gemm_check(M, K, N, G, int4)) return -1;
+    if (gemm_tc_enabled() && gemm_tc_ok(M, K, N, G, int4))
+        return launch_gemm_tc(aq, as, static_cast<const int8_t*>(w), ws, out, resid, M, K, N, G, epi, st);
     GemmArgs g = {aq, as, w, ws, out, resid, M, K, N, G, gemm_gpc(K, G)};
     switch (epi * 2 + (int4 ? 1 : 0)) {
         case kEpiStore * 2: return launch_one<kEpiStore, 0>(g, st);

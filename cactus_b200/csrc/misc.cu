@@ -9,6 +9,14 @@ namespace cb {
 
 __device__ unsigned g_dev_error = 0;
 
+unsigned* dev_error_ptr() {
+    static unsigned* p = [] {
+        void* a = nullptr;
+        return cudaGetSymbolAddress(&a, g_dev_error) == cudaSuccess ? static_cast<unsigned*>(a) : nullptr;
+    }();
+    return p;
+}
+
 // ------------------------------------------------------------------ activation quantization
 // graph_ops_nn.cpp:35-66: per row absmax -> scale = max(absmax/127, 1e-10) -> int8 (RNE).
 __global__ void quantize_act_kernel(const __half* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scales,

@@ -57,10 +57,12 @@ def _weights(rng, N, K, G, int4=False):
 @pytest.mark.parametrize("M,K,N,G", [(1, 1024, 3072, 32), (1, 1024, 3072, 128), (2, 2048, 1000, 64),
                                       (5, 640, 520, 32), (8, 1024, 4096, 128), (13, 3072, 1024, 32),
                                       (1, 8192, 264, 32),
-                                      # M >= 16: the tensor-core GEMM path
+                                      # 16 <= M: the mma.sync GEMM (INT4, M < 64, K % 128 != 0) or the
+                                      # tcgen05 GEMM (INT8, M >= 64, K % 128 == 0, G in 32/64/128)
                                       (16, 1024, 3072, 32), (127, 2048, 1024, 32), (64, 3072, 1024, 128),
                                       (33, 640, 512, 32), (200, 1024, 4096, 64), (17, 576, 960, 32),
-                                      (130, 1024, 96, 128)])
+                                      (130, 1024, 96, 128), (64, 128, 32, 32), (128, 256, 64, 64),
+                                      (300, 896, 4864, 32), (513, 1024, 160, 32), (96, 640, 512, 32)])
 def test_matmul_prequantized_bit_exact(L, ref, int4, M, K, N, G):
     if int4 and G % 32:
         pytest.skip("INT4 groups are multiples of 32")
