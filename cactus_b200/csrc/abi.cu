@@ -312,12 +312,13 @@ CB_API int cactus_cuda_attention_hybrid_int8_fp16(const uint16_t* queries, const
         (reinterpret_cast<uintptr_t>(values_cached) & 7))
         return fail(CB_ERR_ARG, "attention_hybrid: misaligned K/V");
     if (scale == 0.0f) scale = 1.0f / sqrtf((float)head_dim);
-    // The reference-order kernel (bit-exact) is used unless a long context would leave most
-    // SMs idle; then the keys are split across warps (same math, different fp32 rounding).
-    const size_t items = batch_size * num_q_heads * seq_len;
-    const bool exact = (cache_len + new_len) <= 4096 || items >= 2 * cb::kNumSMs;
+    // The reference order (bit-exact): long caches split over the keys inside
+    // launch_attention_hybrid_exact; the non-exact kernel only when neither exact path takes
+    // the shape.
     const long long kc_bs = (long long)(cache_len * num_kv_heads * head_dim);
-    if (!exact || cb::launch_attention_hybrid_exact(H(queries), keys_cached, values_cached, k_scales, v_scales,
+    // the exact kernels stage cached rows with 16-byte copies
+    const bool rows16 = aligned16(keys_cached) && aligned16(values_cached);
+    if (!rows16 || cb::launch_attention_hybrid_exact(H(queries), keys_cached, values_cached, k_scales, v_scales,
                                                      H(keys_new), H(values_new), H(output), (int)batch_size,
                                                      (int)seq_len, (int)cache_len, (int)new_len, (int)num_q_heads,
                                                      (int)num_kv_heads, (int)head_dim, scale,

@@ -319,6 +319,14 @@ int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_
                                   int causal, int qgs, long long kc_bstride, long long sc_bstride, cudaStream_t st,
                                   const int* dstate) {
     const unsigned items = (unsigned)((long long)B * Hq * S);
+    // long caches: the same arithmetic split over the keys (not while the lengths live on the
+    // device or the stream is being captured: the split path sizes a scratch buffer on the host)
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (!dstate && (long long)cache_len + new_len >= kSplitMinKeys && cudaStreamIsCapturing(st, &cap) == cudaSuccess &&
+        cap == cudaStreamCaptureStatusNone &&
+        launch_attention_split(q, kc, vc, ks, vs, kn, vn, o, B, S, cache_len, new_len, Hq, Hkv, D, scale, pos_off,
+                               causal, qgs, kc_bstride, sc_bstride, st) == 0)
+        return 0;
 #define CB_EXACT(DD)                                                                                          \
     {                                                                                                         \
         static bool attr = false;                                                                             \

@@ -71,6 +71,16 @@ int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_
                                   int causal, int qgs, long long kc_bstride, long long sc_bstride, cudaStream_t st,
                                   const int* dstate = nullptr);
 void attention_prepare();  // kernel attributes, called before any graph capture
+// Exact hybrid attention split over the keys for long caches (attention_split.cu): same
+// result bits as launch_attention_hybrid_exact; -1 when the shape or the scratch size is
+// outside its limits (the caller then uses the one-CTA-per-query kernel).
+constexpr long long kSplitMinKeys = 512;
+constexpr size_t kSplitMaxSmem = 227 * 1024;
+constexpr size_t kSplitMaxScratch = size_t(4) << 30;
+int launch_attention_split(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
+                           const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len,
+                           int Hq, int Hkv, int D, float scale, long long pos_off, int causal, int qgs,
+                           long long kc_bstride, long long sc_bstride, cudaStream_t st);
 
 // ---- sampling (sample.cu)
 int launch_sample(const __half* logits, int V, float temperature, float top_p, int top_k, float uniform,
