@@ -210,11 +210,14 @@ int launch_one(const GemmArgs& g, cudaStream_t st) {
 }
 }  // namespace
 
-// CACTUS_B200_GEMM=mma keeps every M >= 16 product on the mma.sync kernel (comparison runs)
+// CACTUS_B200_GEMM=tc routes the INT8 shapes it supports to the tcgen05 kernel (gemm_tc.cu).
+// Off by default: measured on B200 it runs at about half the mma.sync kernel's rate at every
+// M from 128 to 4096 (operand staging through cp.async bounds both; the tcgen05 tile is
+// 128 x 16, so A is re-staged for every 16 output columns).
 bool gemm_tc_enabled() {
     static const bool on = [] {
         const char* e = std::getenv("CACTUS_B200_GEMM");
-        return !(e && std::string(e) == "mma");
+        return e && std::string(e) == "tc";
     }();
     return on;
 }

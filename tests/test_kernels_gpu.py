@@ -1,11 +1,14 @@
 """Kernel-level parity: every C-ABI entry point against the CPU restatement (oracle/).
 
 Integer / byte outputs and the fp16 outputs whose arithmetic is reproduced op-for-op
-(quantized matmul, RMSNorm, RoPE, elementwise, softmax lanes, embedding, argmax) are
-required to be bit-exact. Attention outputs use the north-star tolerance: normwise max
-relative error <= 1e-2 (they differ from the oracle only by expf ulps and the order in
-which the decode kernel merges its warps' online-softmax states).
+(quantized matmul, RMSNorm, RoPE, elementwise, softmax lanes, embedding, argmax, the
+reference-order attention kernels) are required to be bit-exact; attention is also checked
+against the north-star tolerance (normwise max relative error <= 1e-2).
 """
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -156,14 +159,32 @@ def test_attention_f16_parity(L, ref, B, S, Skv, Hq, Hkv, D, off, win):
     assert same_bits(got, exp)
 
 
+def test_matmul_tcgen05_path_bit_exact():
+    """The tcgen05 GEMM (opt-in: CACTUS_B200_GEMM=tc, read once per process) on the INT8 GEMM
+    parity cases above, run in a child pytest process."""
+    env = dict(os.environ, CACTUS_B200_GEMM="tc")
+    r = subprocess.run([sys.executable, "-m", "pytest", os.path.abspath(__file__), "-q", "-m", "gpu", "-p",
+                        "no:cacheprovider", "-k", "matmul_prequantized and False"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+# L_ >= 512: the key-split kernels (attention_split.cu); below: one CTA per query
 @pytest.mark.parametrize("B,S,L_,Hq,Hkv,D", [(1, 1, 127, 16, 8, 128), (1, 1, 1024, 32, 8, 64),
                                              (1, 1, 4096, 4, 1, 256), (1, 4, 60, 16, 8, 128),
-                                             (1, 1, 0, 16, 8, 128)])
+                                             (1, 1, 0, 16, 8, 128), (1, 1, 8191, 16, 8, 128),
+                                             (2, 1, 700, 16, 8, 128), (1, 3, 600, 4, 1, 256),
+                                             (3, 2, 511, 16, 8, 128), (1, 1, 2080, 8, 8, 128)])
 def test_attention_hybrid_parity(L, ref, B, S, L_, Hq, Hkv, D):
-    rng = np.random.default_rng(L_ + Hq)
-    kf, vf = f16(rng, (max(L_, 1), Hkv, D)), f16(rng, (max(L_, 1), Hkv, D))
-    kc, ks = ref.quantize_kv(kf)
-    vc, vs = ref.quantize_kv(vf)
+    rng = np.random.default_rng(L_ + Hq + B)
+    kc = np.zeros((B, max(L_, 1), Hkv, D), np.int8)
+    vc = np.zeros_like(kc)
+    for b in range(B):
+        kq, ksb = ref.quantize_kv(f16(rng, (max(L_, 1), Hkv, D)))
+        vq, vsb = ref.quantize_kv(f16(rng, (max(L_, 1), Hkv, D)))
+        kc[b], vc[b] = kq, vq
+        if b == 0:  # the reference indexes the scales without a batch offset
+            ks, vs = ksb, vsb
     kn, vn = f16(rng, (B, S, Hkv, D)), f16(rng, (B, S, Hkv, D))
     q = f16(rng, (B, S, Hq, D))
     scale = 1.0 / np.sqrt(D)
@@ -171,11 +192,10 @@ def test_attention_hybrid_parity(L, ref, B, S, L_, Hq, Hkv, D):
     cb.check(L.cactus_cuda_attention_hybrid_int8_fp16(
         ptr(dev(q)), ptr(dev(kc)), ptr(dev(vc)), ptr(dev(ks)), ptr(dev(vs)), ptr(dev(kn)), ptr(dev(vn)), ptr(o),
         B, S, L_, S, Hq, Hkv, D, scale, L_, 1, 128, None))
-    exp = ref.attention_hybrid(q, kc[:L_] if L_ else kc[:0], vc[:L_] if L_ else vc[:0], ks, vs, kn, vn, scale, L_)
+    exp = ref.attention_hybrid(q, kc[:, :L_], vc[:, :L_], ks, vs, kn, vn, scale, L_)
     got = host(o, np.float16)
     assert rel_err(got, exp) <= TOL
-    if L_ + S <= 4096:  # reference-order kernel: bit-exact
-        assert same_bits(got, exp)
+    assert same_bits(got, exp)  # reference order at every length
 
 
 @pytest.mark.parametrize("S,H,D,G", [(5, 8, 128, 128), (3, 1, 256, 128), (2, 2, 100, 128)])
