@@ -49,11 +49,14 @@ def parse():
     ap.add_argument("--no-kernel-timing", action="store_true")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only time the GEMV kernel class (one token's projections) and print its roofline")
+    ap.add_argument("--gemv-lm", action="store_true",
+                    help="only time the INT8 GEMV on the lm-head shape (one eager launch per call)")
     ap.add_argument("--layers", type=int, default=0, help="--kernel-only: number of layers (default: all)")
     ap.add_argument("--decode", type=int, default=DECODE, help="decode tokens per request (profiling runs use fewer)")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 5],
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2 (default): the headline decode line; 1 / 5: the matmul / attention sweeps, one "
-                         "JSON line per shape")
+                         "JSON line per shape; 3: Gemma prefill 4096 + decode 256; 4: Llama batched decode "
+                         "sweep (data-parallel over the ranks)")
     return ap.parse_args()
 
 
@@ -354,6 +357,183 @@ def run_config5(args):
     return 0
 
 
+def _engine_for(arch, rank, barrier, context_size, max_batch, device):
+    from cactus_b200 import convert
+    from cactus_b200.engine import Engine
+    os.environ.setdefault("CACTUS_B200_MODELS", "/tmp/cactus_b200_models")
+    folder = convert.default_model_dir(arch, seed=0)
+    if rank == 0:
+        convert.make_model(folder, arch, seed=0)
+    barrier()
+    return Engine(folder, context_size=context_size, max_batch=max_batch, device=device)
+
+
+def run_config3(args):
+    """Config 3: Gemma-3-270m-shaped decoder (INT8 attention, INT4 MLP, FP16 embeddings / lm
+    head, 5:1 local:global attention), one request = a 4096-token random prompt (prefill of
+    4095 rows in 256-row chunks) then 256 greedy decode steps, batch 1, through the engine C
+    ABI. Prefill and decode tok/s from CUDA events on the engine stream; one JSON line."""
+    import torch
+    from cactus_b200 import convert
+    torch.cuda.set_device(0)
+    hbm, bf16, src = _peaks()
+    arch = convert.gemma3_270m(GROUP)
+    P, NEW = 4096, 256
+    eng = _engine_for(arch, 0, torch.cuda.synchronize, P + NEW + 8, 1, 0)
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, arch.vocab_size, P).astype(np.uint32) for _ in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        eng.generate_greedy(prompts[i], NEW)
+    pre = dec = wall = 0.0
+    with ClockSampler(0) as clk:
+        for i in range(args.steps):
+            t0 = time.perf_counter()
+            toks = eng.generate_greedy(prompts[args.warmup + i], NEW)
+            wall += time.perf_counter() - t0
+            st = eng.stats()
+            pre += st["prefill_ms"]
+            dec += st["decode_ms"]
+    assert toks.shape == (NEW,)
+    path = eng.decode_path()
+    eng.close()
+    H, F, D, Hq, Hkv, V = arch.hidden_dim, arch.ffn_intermediate_dim, arch.attention_head_dim, arch.attention_heads, \
+        arch.attention_kv_heads, arch.vocab_size
+    attn_w = (Hq + 2 * Hkv) * D * H + H * Hq * D
+    mlp_w = 3 * F * H
+    avg_ctx = P + NEW / 2
+    dec_bytes = arch.num_layers * (attn_w + mlp_w // 2 + (attn_w + mlp_w) // GROUP * 2) + V * H * 2 + \
+        arch.num_layers * avg_ctx * Hkv * (2 * D + 2 * 4 * ((D + 127) // 128))
+    pre_flops = 2.0 * (P - 1) * arch.num_layers * (attn_w + mlp_w)  # projections; the lm head sees the last row only
+    dec_tok_s = args.steps * NEW / (dec / 1e3)
+    print(json.dumps({
+        "config": 3, "workload": f"gemma3-270m mixed int8/int4 g{GROUP} batch1 prefill{P} decode{NEW}",
+        "prefill_tok_s": args.steps * (P - 1) / (pre / 1e3),
+        "prefill_projection_tflops": pre_flops * args.steps / (pre / 1e3) / 1e12,
+        "decode_tok_s": dec_tok_s,
+        "decode_bytes_per_token": dec_bytes,
+        "decode_achieved_gbs": dec_bytes * dec_tok_s / 1e9, "decode_frac_of_hbm": dec_bytes * dec_tok_s / 1e9 / hbm,
+        "e2e_tok_s": args.steps * NEW / wall,
+        "decode_path": {0: "host loop", 1: "cuda graph of per-op kernels", 2: "persistent step"}[path],
+        "peak_source": src, "clocks": clk.summary(),
+        "data": "synthetic (random-init N(0,0.02) weights, random prompt ids)"}), flush=True)
+    return 0
+
+
+def run_config4(args):
+    """Config 4: Llama-3.2-1B-shaped decoder (INT4 group-32 weights), batched greedy decode of B
+    independent sequences, each with a 1024-token random context (full cache: window 0), split
+    data-parallel across the ranks (contiguous shards, no collective on the data path). One JSON
+    line per B in {1, 8, 64, 256}: aggregate decode tok/s = B * steps / max-over-ranks decode time."""
+    import torch
+    from cactus_b200 import convert, dist
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local_rank))
+        pg = tdist
+
+    def barrier():
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    hbm, _, src = _peaks()
+    arch = convert.llama3_2_1b(GROUP)
+    P, NEW, BMAX = 1024, 32, 256
+    shard_max = -(-BMAX // world)
+    eng = _engine_for(arch, rank, barrier, P + NEW + 8, shard_max, local_rank)
+    eng.set_cache_window(0, 0)
+    H, F, D, Hq, Hkv, V = arch.hidden_dim, arch.ffn_intermediate_dim, arch.attention_head_dim, arch.attention_heads, \
+        arch.attention_kv_heads, arch.vocab_size
+    w = arch.num_layers * ((Hq + 2 * Hkv) * D * H + H * Hq * D + 3 * F * H) + V * H
+    step_w_bytes = w // 2 + w // GROUP * 2
+    kv_seq = arch.num_layers * (P + NEW / 2) * Hkv * (2 * D + 2 * 4 * ((D + 127) // 128))
+    for B in (1, 8, 64, 256):
+        s0, s1 = dist.shard(B, rank, world)
+        bg = s1 - s0
+        rng = np.random.default_rng(4000 + B)
+        prompts = rng.integers(0, V, (B, P)).astype(np.uint32)[s0:s1]
+        dec = pre = 0.0
+        for it in range(args.warmup + args.steps):
+            if bg:
+                if bg == 1:
+                    eng.generate_greedy(prompts[0], NEW)
+                else:
+                    eng.generate_batch_greedy(prompts, NEW)
+                st = eng.stats()
+                if it >= args.warmup:
+                    dec += st["decode_ms"]
+                    pre += st["prefill_ms"]
+        t = torch.tensor([dec, pre], dtype=torch.float64, device="cuda")
+        if pg:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        barrier()
+        if rank == 0:
+            dmax, pmax = t[0].item(), t[1].item()
+            tok_s = B * NEW * args.steps / (dmax / 1e3)
+            per_gpu_bytes = step_w_bytes + kv_seq * shard_max if B >= world else step_w_bytes + kv_seq
+            step_s = dmax / 1e3 / (args.steps * NEW)
+            print(json.dumps({
+                "config": 4, "workload": f"llama3.2-1b int4 g{GROUP} batched decode B={B} ctx{P} (+{NEW} steps)",
+                "n_gpus": world, "batch_per_gpu": -(-B // world), "decode_tok_s": tok_s,
+                "prefill_tok_s": B * (P - 1) * args.steps / (pmax / 1e3),
+                "ms_per_decode_step": step_s * 1e3,
+                "per_gpu_bytes_per_step": per_gpu_bytes,
+                "per_gpu_achieved_gbs": per_gpu_bytes / step_s / 1e9,
+                "per_gpu_frac_of_hbm": per_gpu_bytes / step_s / 1e9 / hbm, "peak_source": src,
+                "parallelism": f"dp{world} (contiguous sequence shards, no collective)",
+                "data": "synthetic (random-init N(0,0.02) weights, random context ids)"}), flush=True)
+    eng.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def run_gemv_lm(args):
+    """The grouped INT8 GEMV alone on the Qwen3-0.6B lm-head shape (M=1, K=1024, N=151936,
+    G=32: 165.3 MB of weights + scales, above the 126 MB L2; two weight copies alternate), one
+    eager launch per call through cactus_cuda_linear_int8, CUDA events per launch."""
+    import torch
+    import cactus_b200 as cb
+    L = cb.lib()
+    torch.cuda.set_device(0)
+    hbm, _, src = _peaks()
+    M, K, N, G = 1, 1024, 151936, GROUP
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    ws = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g) for _ in range(2)]
+    ss = [(torch.rand((N, K // G), device="cuda", generator=g) * 1e-3).half() for _ in range(2)]
+    x = torch.randn((M, K), device="cuda", generator=g).half()
+    y = torch.empty((M, N), device="cuda", dtype=torch.half)
+    st = torch.cuda.current_stream().cuda_stream
+
+    def call(i):
+        cb.check(L.cactus_cuda_linear_int8(x.data_ptr(), ws[i % 2].data_ptr(), ss[i % 2].data_ptr(), y.data_ptr(),
+                                           M, K, N, G, st), "linear_int8")
+    for i in range(max(args.warmup, 3)):
+        call(i)
+    times = []
+    for i in range(max(args.steps, 5)):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call(i)
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = sorted(times)[len(times) // 2]
+    nbytes = N * K + N * (K // G) * 2 + M * K * 2 + M * N * 2
+    print(json.dumps({"config": 1, "workload": f"int8 linear M={M} K={K} N={N} G={G} (lm-head shape)",
+                      "us_per_matmul": ms * 1e3, "algorithmic_bytes": nbytes,
+                      "achieved_gbs": nbytes / (ms / 1e3) / 1e9, "frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / hbm,
+                      "peak_source": src, "l2": "two alternating weight copies of 165 MB > L2"}), flush=True)
+    return 0
+
+
 def run_kernel_only(args):
     import torch
     from cactus_b200 import convert
@@ -377,10 +557,16 @@ def main():
         return run_reference(args)
     if args.kernel_only:
         return run_kernel_only(args)
+    if args.gemv_lm:
+        return run_gemv_lm(args)
     if args.config == 1:
         return run_config1(args)
     if args.config == 5:
         return run_config5(args)
+    if args.config == 3:
+        return run_config3(args)
+    if args.config == 4:
+        return run_config4(args)
     import torch
     rank, local_rank, world = dist_env()
     torch.cuda.set_device(local_rank)
