@@ -475,7 +475,7 @@ def run_config4(args):
         if rank == 0:
             dmax, pmax = t[0].item(), t[1].item()
             tok_s = B * NEW * args.steps / (dmax / 1e3)
-            per_gpu_bytes = step_w_bytes + kv_seq * shard_max if B >= world else step_w_bytes + kv_seq
+            per_gpu_bytes = step_w_bytes + kv_seq * -(-B // world)
             step_s = dmax / 1e3 / (args.steps * NEW)
             print(json.dumps({
                 "config": 4, "workload": f"llama3.2-1b int4 g{GROUP} batched decode B={B} ctx{P} (+{NEW} steps)",

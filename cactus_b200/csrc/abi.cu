@@ -118,10 +118,13 @@ static int gemv_or_chunks(cb::GemvCall c, size_t M, size_t K, size_t N, size_t G
     c.K = (int)K;
     c.N = (int)N;
     c.G = (int)G;
-    // rows beyond 8 are processed in chunks of 8 (the weights are re-read from L2)
-    for (size_t m0 = 0; m0 < M; m0 += 8) {
+    // rows beyond one launch's limit (8, fewer for very large K) are processed in chunks
+    // (the weights are re-read from L2)
+    const size_t per = (size_t)cb::gemv_rows_per_launch(c.int4, c.pro, c.K, c.G);
+    if (per == 0) return fail(CB_ERR_ARG, std::string(name) + ": gemv: K too large for the shared-memory tile");
+    for (size_t m0 = 0; m0 < M; m0 += per) {
         cb::GemvCall cc = c;
-        cc.M = (int)((M - m0) < 8 ? (M - m0) : 8);
+        cc.M = (int)((M - m0) < per ? (M - m0) : per);
         if (cc.x) cc.x = c.x + m0 * K;
         if (cc.aq) cc.aq = c.aq + m0 * K;
         if (cc.as) cc.as = c.as + m0;

@@ -52,7 +52,17 @@ struct SplitArgs {
     long long kc_bstride, sc_bstride, pos_off, lw, nbw;
     int S, cache_len, new_len, Hq, Hkv, causal, qgs;
     float scale;
+    const int* dstate;  // non-null: cache_len = dstate[0], pos_off = dstate[1] (read on the device)
 };
+
+// Lengths that live on the device (CUDA-graph decode): read after griddepcontrol.wait, since
+// the previous kernels of the step may still be advancing them.
+__device__ __forceinline__ void split_lengths(SplitArgs& a) {
+    if (a.dstate) {
+        a.cache_len = __ldcg(a.dstate);
+        a.pos_off = __ldcg(a.dstate + 1);
+    }
+}
 
 __device__ __forceinline__ long long split_kv_end(const SplitArgs& a, int qp) {
     const long long kv_seq_len = (long long)a.cache_len + a.new_len;
@@ -77,6 +87,7 @@ template <int D>
 __global__ void __launch_bounds__(kS1Threads) attn_split_scores_kernel(SplitArgs a) {
     pdl_launch_dependents();
     pdl_wait();
+    split_lengths(a);
     extern __shared__ __align__(16) uint8_t smem[];
     const int grp = a.Hq / a.Hkv;
     const long long gi = blockIdx.x;
@@ -178,6 +189,7 @@ template <int D>
 __global__ void __launch_bounds__(D) attn_split_chain_kernel(SplitArgs a) {
     pdl_launch_dependents();
     pdl_wait();
+    split_lengths(a);
     extern __shared__ __align__(16) uint8_t smem[];
     constexpr int SB = s2_stage_bytes<D>();
     const long long item = blockIdx.x;
@@ -337,46 +349,61 @@ float* split_scratch(size_t bytes) {
 }
 
 template <int D>
-int launch_split(SplitArgs a, long long items, long long kv_seq_len, int B, cudaStream_t st) {
-    const int grp = a.Hq / a.Hkv;
-    const size_t sm1 = (size_t)s1_smem<D>(grp);
-    const size_t sm2 = (size_t)kS2Stages * s2_stage_bytes<D>() + (size_t)4 * a.nbw * 4;
-    if (sm1 > kSplitMaxSmem || sm2 > kSplitMaxSmem) return -1;
+bool split_attrs(size_t sm1, size_t sm2) {
+    static std::mutex mu;
     static size_t attr1 = 0, attr2 = 0;
+    std::lock_guard<std::mutex> lk(mu);
     if (sm1 > attr1) {
         if (cudaFuncSetAttribute(attn_split_scores_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1) !=
             cudaSuccess)
-            return -1;
+            return false;
         attr1 = sm1;
     }
     if (sm2 > attr2) {
         if (cudaFuncSetAttribute(attn_split_chain_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2) !=
             cudaSuccess)
-            return -1;
+            return false;
         attr2 = sm2;
     }
+    return true;
+}
+
+template <int D>
+size_t split_sm1(int grp) { return (size_t)s1_smem<D>(grp); }
+template <int D>
+size_t split_sm2(long long nbw) { return (size_t)kS2Stages * s2_stage_bytes<D>() + (size_t)4 * nbw * 4; }
+
+// size_keys: keys the grid and the scratch rows are sized for (the live length, or with
+// device-side lengths the largest one the launch may see)
+template <int D>
+int launch_split(SplitArgs a, long long items, long long size_keys, int B, cudaStream_t st) {
+    const int grp = a.Hq / a.Hkv;
+    const size_t sm1 = split_sm1<D>(grp), sm2 = split_sm2<D>(a.nbw);
+    if (sm1 > kSplitMaxSmem || sm2 > kSplitMaxSmem) return -1;
+    if (!split_attrs<D>(sm1, sm2)) return -1;
     const long long kv_items = (long long)B * a.S * a.Hkv;
-    const long long nchunk = (kv_seq_len + kS1Keys - 1) / kS1Keys;
+    const long long nchunk = (size_keys + kS1Keys - 1) / kS1Keys;
     if (kv_items > 0x7FFFFFFFLL || nchunk > 65535 || items > 0x7FFFFFFFLL) return -1;
     launch_k(attn_split_scores_kernel<D>, dim3((unsigned)kv_items, (unsigned)nchunk), dim3(kS1Threads), sm1, st, a);
     launch_k(attn_split_chain_kernel<D>, dim3((unsigned)items), dim3(D), sm2, st, a);
     return 0;
 }
 
-}  // namespace
+long long split_lw(long long keys) { return (keys + kS2Keys - 1) / kS2Keys * kS2Keys; }
 
-int launch_attention_split(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
-                           const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len,
-                           int Hq, int Hkv, int D, float scale, long long pos_off, int causal, int qgs,
-                           long long kc_bstride, long long sc_bstride, cudaStream_t st) {
+int split_common(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
+                 const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len, int Hq,
+                 int Hkv, int D, float scale, long long pos_off, int causal, int qgs, long long kc_bstride,
+                 long long sc_bstride, long long size_keys, const int* dstate, float* scr, size_t scr_bytes,
+                 cudaStream_t st) {
     if (B < 1 || S < 1 || Hkv < 1 || Hq % Hkv || qgs % 8 || (D + qgs - 1) / qgs > 2) return -1;
-    const long long kv_seq_len = (long long)cache_len + new_len;
-    const long long lw = (kv_seq_len + kS2Keys - 1) / kS2Keys * kS2Keys;
+    const long long lw = split_lw(size_keys);
     const long long nbw = lw / 32;
     const long long items = (long long)B * S * Hq;
     const size_t bytes = (size_t)items * (size_t)(lw + 3 * nbw) * 4;
     if (bytes > kSplitMaxScratch) return -1;
-    float* scr = split_scratch(bytes);
+    if (!scr) scr = split_scratch(bytes);
+    else if (bytes > scr_bytes) return -1;
     if (!scr) return -1;
     SplitArgs a;
     a.q = q;
@@ -404,12 +431,54 @@ int launch_attention_split(const __half* q, const int8_t* kc, const int8_t* vc, 
     a.causal = causal;
     a.qgs = qgs;
     a.scale = scale;
+    a.dstate = dstate;
     switch (D) {
-        case 64: return launch_split<64>(a, items, kv_seq_len, B, st);
-        case 128: return launch_split<128>(a, items, kv_seq_len, B, st);
-        case 256: return launch_split<256>(a, items, kv_seq_len, B, st);
+        case 64: return launch_split<64>(a, items, size_keys, B, st);
+        case 128: return launch_split<128>(a, items, size_keys, B, st);
+        case 256: return launch_split<256>(a, items, size_keys, B, st);
     }
     return -1;
+}
+
+}  // namespace
+
+int launch_attention_split(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
+                           const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len,
+                           int Hq, int Hkv, int D, float scale, long long pos_off, int causal, int qgs,
+                           long long kc_bstride, long long sc_bstride, cudaStream_t st) {
+    return split_common(q, kc, vc, ks, vs, kn, vn, o, B, S, cache_len, new_len, Hq, Hkv, D, scale, pos_off, causal,
+                        qgs, kc_bstride, sc_bstride, (long long)cache_len + new_len, nullptr, nullptr, 0, st);
+}
+
+size_t attention_split_scratch_bytes(long long items, long long max_keys) {
+    const long long lw = split_lw(max_keys);
+    return (size_t)items * (size_t)(lw + 3 * (lw / 32)) * 4;
+}
+
+int attention_split_prepare(int D, int Hq, int Hkv, long long max_keys) {
+    if (Hkv < 1 || Hq % Hkv) return -1;
+    const long long nbw = split_lw(max_keys) / 32;
+    const int grp = Hq / Hkv;
+    bool ok = false;
+    switch (D) {
+        case 64: ok = split_sm1<64>(grp) <= kSplitMaxSmem && split_sm2<64>(nbw) <= kSplitMaxSmem &&
+                      split_attrs<64>(split_sm1<64>(grp), split_sm2<64>(nbw)); break;
+        case 128: ok = split_sm1<128>(grp) <= kSplitMaxSmem && split_sm2<128>(nbw) <= kSplitMaxSmem &&
+                       split_attrs<128>(split_sm1<128>(grp), split_sm2<128>(nbw)); break;
+        case 256: ok = split_sm1<256>(grp) <= kSplitMaxSmem && split_sm2<256>(nbw) <= kSplitMaxSmem &&
+                       split_attrs<256>(split_sm1<256>(grp), split_sm2<256>(nbw)); break;
+    }
+    return ok ? 0 : -1;
+}
+
+int launch_attention_split_dev(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
+                               const __half* kn, const __half* vn, __half* o, int B, int S, int new_len, int Hq,
+                               int Hkv, int D, float scale, int causal, int qgs, long long kc_bstride,
+                               long long sc_bstride, long long max_keys, const int* dstate, float* scratch,
+                               size_t scratch_bytes, cudaStream_t st) {
+    if (!dstate || !scratch) return -1;
+    return split_common(q, kc, vc, ks, vs, kn, vn, o, B, S, 0, new_len, Hq, Hkv, D, scale, 0, causal, qgs, kc_bstride,
+                        sc_bstride, max_keys, dstate, scratch, scratch_bytes, st);
 }
 
 }  // namespace cb

@@ -298,6 +298,10 @@ void Engine::init(const std::string& folder, size_t context_size, size_t max_bat
     hist_dev_ = static_cast<uint32_t*>(dmalloc(128 * 4, owned_));
     sample_work_ = static_cast<__half*>(dmalloc((size_t)V_ * 2, owned_));
     f32_scratch_ = static_cast<float*>(dmalloc(64, owned_));
+    if ((long long)cap_ + 1 >= kSplitMinKeys && attention_split_prepare(D_, Hq_, Hkv_, (long long)cap_ + 1) == 0) {
+        split_scr_bytes_ = attention_split_scratch_bytes((long long)max_batch_ * Hq_, (long long)cap_ + 1);
+        split_scr_ = static_cast<float*>(dmalloc(split_scr_bytes_, owned_));
+    }
 
     // RoPE tables per layer (Gemma: global every 6th layer theta 1e6, local 1e4; model_gemma.cpp:84-88)
     ct_.assign(L_, nullptr);
@@ -422,7 +426,9 @@ void Engine::gemv(const Mat& w, int pro, int epi, const __half* x, const __half*
         launches_ += 2;
         return;
     }
-    for (int m0 = 0; m0 < M; m0 += 8) {
+    const int per = gemv_rows_per_launch(w.prec == kInt4 ? 1 : 0, pro, w.K, w.G);
+    if (per == 0) throw std::runtime_error("gemv: K too large for the shared-memory tile");
+    for (int m0 = 0; m0 < M; m0 += per) {
         GemvCall c = {};
         c.int4 = w.prec == kInt4 ? 1 : 0;
         c.pro = pro;
@@ -435,7 +441,7 @@ void Engine::gemv(const Mat& w, int pro, int epi, const __half* x, const __half*
         const int outN = (epi == kEpiGluSilu || epi == kEpiGluGelu) ? w.N / 2 : w.N;
         c.out = out + (size_t)m0 * outN;
         c.resid = resid ? resid + (size_t)m0 * outN : nullptr;
-        c.M = std::min(8, M - m0);
+        c.M = std::min(per, M - m0);
         c.K = w.K;
         c.N = w.N;
         c.G = w.G;
@@ -494,8 +500,15 @@ void Engine::forward(int B, int S, bool graph_mode) {
             launch_attention_f16(q_, kl, vl, attn_, B, S, S, Hq_, Hkv_, D_, attention_scale_, (long long)total_len_,
                                  win, 1, stream_);
         } else {
-            // reference-order (bit-exact) hybrid attention (kernel_attention.cpp:257-482)
-            if (launch_attention_hybrid_exact(q_, kcl, vcl, ksl, vsl, kl, vl, attn_, B, S, (int)cache_len_, S, Hq_,
+            // reference-order (bit-exact) hybrid attention (kernel_attention.cpp:257-482); in a
+            // decode graph over a long cache the same arithmetic split over the keys
+            if (graph_mode && split_graph_ && S == 1) {
+                if (launch_attention_split_dev(q_, kcl, vcl, ksl, vsl, kl, vl, attn_, B, S, S, Hq_, Hkv_, D_,
+                                               attention_scale_, 1, 128, cache_bstride_, scale_bstride_,
+                                               (long long)cap_ + 1, ds, split_scr_, split_scr_bytes_, stream_) != 0)
+                    throw std::runtime_error("split attention launch failed");
+                ++launches_;
+            } else if (launch_attention_hybrid_exact(q_, kcl, vcl, ksl, vsl, kl, vl, attn_, B, S, (int)cache_len_, S, Hq_,
                                               Hkv_, D_, attention_scale_, (long long)total_len_, 1, 128,
                                               cache_bstride_, scale_bstride_, stream_, ds) != 0)
                 throw std::runtime_error("unsupported head_dim for the hybrid attention kernel");
@@ -825,15 +838,30 @@ void Engine::generate(const uint32_t* prompts, int B, size_t P, size_t max_new, 
             launches_ += 2;
         }
     } else {
-        if (!graph_exec_ || graph_batch_ != B || graph_ring_ != ring_ || graph_ring_stride_ != (int)max_new) {
+        // long caches decode through the key-split attention (two kernels, exact); the choice is
+        // part of the captured graph
+        const bool want_split = split_scr_ && (long long)cache_len_ + 1 >= kSplitMinKeys &&
+                                attention_split_scratch_bytes((long long)B * Hq_, (long long)cap_ + 1) <= split_scr_bytes_;
+        if (!graph_exec_ || graph_batch_ != B || graph_ring_ != ring_ || graph_ring_stride_ != (int)max_new ||
+            graph_split_ != want_split) {
             if (graph_exec_) {
                 cudaGraphExecDestroy(graph_exec_);
                 graph_exec_ = nullptr;
             }
             cudaGraph_t g = nullptr;
+            split_graph_ = want_split;
             ck(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "capture");
-            decode_step_device(B, ring_, (int)max_new, true);
+            try {
+                decode_step_device(B, ring_, (int)max_new, true);
+            } catch (...) {
+                split_graph_ = false;
+                cudaStreamEndCapture(stream_, &g);
+                if (g) cudaGraphDestroy(g);
+                throw;
+            }
             ck(cudaStreamEndCapture(stream_, &g), "end capture");
+            split_graph_ = false;
+            graph_split_ = want_split;
             ck(cudaGraphInstantiate(&graph_exec_, g, 0), "instantiate");
             ck(cudaGraphGetNodes(g, nullptr, &graph_nodes_), "graph nodes");
             cudaGraphDestroy(g);

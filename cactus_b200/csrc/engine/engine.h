@@ -137,6 +137,11 @@ private:
     float* f32_scratch_ = nullptr;
     size_t ring_cap_ = 0;
     std::vector<const __half*> ct_, st_;
+    // exact key-split attention inside decode graphs (long caches): scratch sized for the
+    // capacity; split_graph_ selects it while a decode graph is captured
+    float* split_scr_ = nullptr;
+    size_t split_scr_bytes_ = 0;
+    bool split_graph_ = false, graph_split_ = false;
     cudaGraphExec_t graph_exec_ = nullptr;
     size_t graph_nodes_ = 0;
     cudaEvent_t ev_[3] = {nullptr, nullptr, nullptr};

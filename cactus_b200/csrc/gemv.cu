@@ -60,6 +60,16 @@ bool g_attr_set[2][9][5][kNumCombos] = {};
 
 }  // namespace
 
+constexpr int kSmemLimit = 227 * 1024;
+
+int gemv_rows_per_launch(int int4, int pro, int K, int G) {
+    for (int mt = 8; mt >= 1; mt >>= 1)
+        if (gemv_layout(int4, mt, 1, 2, pro, K, G).total <= kSmemLimit) return mt;
+    return 0;
+}
+
+static int mt_of(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+
 const char* gemv_check(const GemvCall& c) {
     if (c.M < 1 || c.M > 8) return "gemv: M must be in [1, 8]";
     if (c.N < 1 || c.K < 1 || c.G < 1) return "gemv: empty shape";
@@ -70,8 +80,8 @@ const char* gemv_check(const GemvCall& c) {
         return "gemv: weights and scales must be 16-byte aligned";
     if ((c.epi == kEpiGluSilu || c.epi == kEpiGluGelu) && (c.N & 1)) return "gemv: GLU epilogue needs even N";
     if (combo_index(c.pro, c.epi) < 0) return "gemv: unsupported prologue/epilogue combination";
-    const GemvLayout L = gemv_layout(c.int4, 8, 1, 2, c.pro, c.K, c.G);
-    if (L.total > 227 * 1024) return "gemv: K too large for the shared-memory tile";
+    const GemvLayout L = gemv_layout(c.int4, mt_of(c.M), 1, 2, c.pro, c.K, c.G);
+    if (L.total > kSmemLimit) return "gemv: K too large for the shared-memory tile";
     return nullptr;
 }
 
@@ -93,10 +103,11 @@ void gemv_prepare() {
 }
 
 int launch_gemv(const GemvCall& c, cudaStream_t st) {
-    const int mt = c.M <= 1 ? 1 : c.M <= 2 ? 2 : c.M <= 4 ? 4 : 8;
+    const int mt = mt_of(c.M);
     // rows per tile: 8 for narrow outputs (>= 128 tiles at N = 1024), 16 for mid-size, 32 for
-    // very wide ones (the vocabulary projection)
-    const int rpw = c.N >= 32 * 2 * kNumSMs ? 4 : (c.N >= 16 * kNumSMs ? 2 : 1);
+    // very wide ones (the vocabulary projection); fewer when two stages would not fit
+    int rpw = c.N >= 32 * 2 * kNumSMs ? 4 : (c.N >= 16 * kNumSMs ? 2 : 1);
+    while (rpw > 1 && gemv_layout(c.int4, mt, rpw, 2, c.pro, c.K, c.G).total > kSmemLimit) rpw >>= 1;
     const int R = 8 * rpw;
     const int ntiles = (c.N + R - 1) / R;
     int S = 4;
@@ -105,7 +116,7 @@ int launch_gemv(const GemvCall& c, cudaStream_t st) {
         --S;
         L = gemv_layout(c.int4, mt, rpw, S, c.pro, c.K, c.G);
     }
-    if (L.total > 227 * 1024) return -1;
+    if (L.total > kSmemLimit) return -1;
     const int per_sm = L.total <= 112 * 1024 ? 2 : 1;
     const int grid = ntiles < per_sm * kNumSMs ? ntiles : per_sm * kNumSMs;
     const int ci = combo_index(c.pro, c.epi);

@@ -29,6 +29,9 @@ struct GemvCall {
 int launch_gemv(const GemvCall& c, cudaStream_t st);
 void gemv_prepare();  // set kernel attributes of all variants (call before graph capture)
 const char* gemv_check(const GemvCall& c);  // nullptr when the shape is supported
+// Largest number of activation rows (8, 4, 2 or 1) one GEMV launch takes for this weight
+// format / prologue / K / G within the shared-memory limit (0: not even one row fits).
+int gemv_rows_per_launch(int int4, int pro, int K, int G);
 
 // ---- grouped INT8 / INT4 GEMM for M >= 16 on the tensor cores (gemm.cu); A pre-quantised
 const char* gemm_check(int M, int K, int N, int G, int int4);  // nullptr when supported
@@ -81,6 +84,18 @@ int launch_attention_split(const __half* q, const int8_t* kc, const int8_t* vc, 
                            const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len,
                            int Hq, int Hkv, int D, float scale, long long pos_off, int causal, int qgs,
                            long long kc_bstride, long long sc_bstride, cudaStream_t st);
+// The same split with the lengths read on the device from dstate = [cache_len, total_len]
+// (CUDA-graph decode: one captured launch serves every step). The grid and the caller-owned
+// scratch (attention_split_scratch_bytes(B*S*Hq, max_keys) bytes) are sized for max_keys keys;
+// blocks past the live length return at once. attention_split_prepare sets the kernels'
+// shared-memory limits for max_keys (call it before any stream capture).
+size_t attention_split_scratch_bytes(long long items, long long max_keys);
+int attention_split_prepare(int D, int Hq, int Hkv, long long max_keys);
+int launch_attention_split_dev(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
+                               const __half* kn, const __half* vn, __half* o, int B, int S, int new_len, int Hq,
+                               int Hkv, int D, float scale, int causal, int qgs, long long kc_bstride,
+                               long long sc_bstride, long long max_keys, const int* dstate, float* scratch,
+                               size_t scratch_bytes, cudaStream_t st);
 
 // ---- sampling (sample.cu)
 int launch_sample(const __half* logits, int V, float temperature, float top_p, int top_k, float uniform,

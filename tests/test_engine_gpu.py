@@ -107,6 +107,41 @@ def test_batched_sequences_are_independent(folders):
     eng.close()
 
 
+def test_batched_llama_ffn_width_matches_oracle(tmp_path_factory):
+    """Llama-3.2-1B's FFN width (8192, INT4 G32): the down projection's K = 8192 limits one GEMV
+    launch to 4 activation rows, so a batch of 6 runs it in row chunks."""
+    arch = convert.tiny("smol", layers=1, hidden=256, ffn=8192, heads=4, kv_heads=2, head_dim=64,
+                        precision={"attn": "INT4", "mlp": "INT4", "embed": "INT4"}, theta=5e5)
+    folder = convert.make_model(str(tmp_path_factory.mktemp("llama_ffn")), arch, seed=5, norm_std=0.1)
+    prompts = np.random.default_rng(11).integers(0, 1000, (6, 7)).astype(np.uint32)
+    eng = Engine(folder, context_size=128, max_batch=6)
+    batch = eng.generate_batch_greedy(prompts, 6)
+    eng.close()
+    ref = OM.RefModel(folder, context_size=128)
+    for b in range(6):
+        assert batch[b].tolist() == ref.generate_greedy(prompts[b].tolist(), 6)
+
+
+@pytest.mark.parametrize("kind,batch", [("gemma", 1), ("smol", 3)])
+def test_graph_decode_over_long_cache_matches_oracle(folders, kind, batch):
+    """Decode graphs over caches of 512+ keys run the exact key-split attention with the
+    lengths read on the device; tokens must equal the oracle's for every sequence."""
+    folder = folders[kind]
+    P = 530
+    prompts = np.random.default_rng(12).integers(0, 1000, (batch, P)).astype(np.uint32)
+    ref = OM.RefModel(folder, context_size=600, window=0, sink=0)
+    exp = [ref.generate_greedy(prompts[b].tolist(), 6) for b in range(batch)]
+    eng = Engine(folder, context_size=600, max_batch=batch)
+    eng.set_cache_window(0, 0)
+    got = eng.generate_batch_greedy(prompts, 6) if batch > 1 else eng.generate_greedy(prompts[0], 6)[None]
+    assert eng.decode_path() == 1  # the CUDA-graph decode
+    for b in range(batch):
+        assert got[b].tolist() == exp[b]
+    if batch == 1:
+        assert _rel(eng.last_logits(), ref.last_logits) <= TOL
+    eng.close()
+
+
 PERSISTENT_KINDS = {
     "qwen": lambda: convert.tiny("qwen", layers=2),
     "qwen_g128": lambda: convert.tiny("qwen", layers=2, group_size=128),

@@ -97,6 +97,20 @@ def test_config1_graph_matmul_bit_exact(L, ref, int4, M):
     assert rel_err(got, exp) <= TOL
 
 
+@pytest.mark.parametrize("int4", [False, True])
+@pytest.mark.parametrize("M", [1, 5, 8, 12])
+def test_linear_llama_down_projection_bit_exact(L, ref, int4, M):
+    """Llama-3.2-1B down projection (K = 8192, N = 2048, G = 32) with fused activation
+    quantisation: the rows one GEMV launch holds shrink with K, so M > 4 runs in chunks."""
+    rng = np.random.default_rng(8192 + M)
+    B, Bs = _weights(rng, 2048, 8192, 32, int4)
+    x = f16(rng, (M, 8192))
+    C = empty((M, 2048), np.float16)
+    fn = L.cactus_cuda_linear_int4 if int4 else L.cactus_cuda_linear_int8
+    cb.check(fn(ptr(dev(x)), ptr(dev(B)), ptr(dev(Bs)), ptr(C), M, 8192, 2048, 32, None))
+    assert same_bits(host(C, np.float16), ref.linear_fp16_act(x, B, Bs, 32, int4=int4))
+
+
 def test_matmul_rejects_bad_shapes(L):
     rng = np.random.default_rng(1)
     B, Bs = _weights(rng, 16, 96, 32)
