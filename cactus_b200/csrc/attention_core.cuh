@@ -7,7 +7,7 @@
 // The recurrence only chains the per-block (max, sum) pair and the per-dim accumulator;
 // scores, block maxima, weights and block sums of a block depend on that block alone. So a
 // chunk of CH keys is processed in phases:
-//   1. all scores in parallel (8-lane dot products in the reference lane order),
+//   1. all scores in parallel (one thread per key keeps the reference's 8 lane accumulators),
 //   2. per 32-key block (one warp each): max, weights expf(s - max), in-order block sum,
 //   3. per output dim (one thread each): walk the blocks in order applying the correction
 //      expf(run_max - block_max) and the in-order V FMAs — the same operation sequence, so
@@ -33,10 +33,17 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// Row stride of the staged INT8 keys: 16 bytes of padding put the rows that eight consecutive
+// threads read with 16-byte loads into eight different bank groups.
+template <int D>
+__host__ __device__ constexpr int attn_krow() {
+    return D + 16;
+}
+
 // shared-memory footprint of attn_exact_core<D, CH> (a multiple of 16 bytes)
 template <int D, int CH>
 __host__ __device__ constexpr int attn_core_smem() {
-    return 2 * CH * D + (CH * 2 * 2 + CH + 3 * (CH / 32)) * 4;
+    return CH * attn_krow<D>() + CH * D + (CH * 2 * 2 + CH + 3 * (CH / 32)) * 4;
 }
 
 struct SyncBlock {
@@ -64,8 +71,9 @@ struct AttnCoreArgs {
 // commits them as one group (all NT threads call it).
 template <int D, int NT, int CH>
 __device__ __forceinline__ void attn_stage_chunk(const AttnCoreArgs& a, uint8_t* smem, long long c0) {
+    constexpr int KR = attn_krow<D>();
     int8_t* kraw = reinterpret_cast<int8_t*>(smem);
-    int8_t* vraw = kraw + CH * D;
+    int8_t* vraw = kraw + CH * KR;
     float* ksc = reinterpret_cast<float*>(vraw + CH * D);
     float* vsc = ksc + CH * 2;
     const int t = threadIdx.x;
@@ -75,7 +83,7 @@ __device__ __forceinline__ void attn_stage_chunk(const AttnCoreArgs& a, uint8_t*
     for (int c = t; c < ncached * (D / 16); c += NT) {
         const int i = c / (D / 16), off = (c % (D / 16)) * 16;
         const size_t src = (size_t)(c0 + i) * a.kv_row + off;
-        cp_async16(kraw + i * D + off, a.Kc + src);
+        cp_async16(kraw + i * KR + off, a.Kc + src);
         cp_async16(vraw + i * D + off, a.Vc + src);
     }
     for (int c = t; c < ncached * nqg; c += NT) {
@@ -91,8 +99,9 @@ __device__ __forceinline__ void attn_stage_chunk(const AttnCoreArgs& a, uint8_t*
 template <int D, int NT, int CH, class Bar>
 __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t* smem, Bar bar) {
     static_assert(NT % 32 == 0 && NT >= D && NT >= 32 * (CH / 32), "thread count");
-    int8_t* kraw = reinterpret_cast<int8_t*>(smem);   // [CH][D]
-    int8_t* vraw = kraw + CH * D;                       // [CH][D]
+    constexpr int KR = attn_krow<D>();
+    int8_t* kraw = reinterpret_cast<int8_t*>(smem);   // [CH][KR]
+    int8_t* vraw = kraw + CH * KR;                      // [CH][D]
     float* ksc = reinterpret_cast<float*>(vraw + CH * D);  // [CH][2]
     float* vsc = ksc + CH * 2;                          // [CH][2]
     float* sc = vsc + CH * 2;                           // [CH] scores, then weights
@@ -103,7 +112,6 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
     const float* qs = a.qs;
     const int vg = t < D ? t / a.qgs : 0;  // V scale group of this thread's dim
     float acc = 0.0f, run_max = -INFINITY, run_sum = 0.0f;
-    constexpr int KPR = NT / 8;                 // keys per scoring round
 
     for (long long c0 = 0; c0 < a.kv_end; c0 += CH) {
         const int n = (int)min((long long)CH, a.kv_end - c0);
@@ -112,34 +120,41 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
         if (!(c0 == 0 && a.prestaged)) attn_stage_chunk<D, NT, CH>(a, smem, c0);
         cp_async_wait<0>();
         bar();
-        // phase 1: scores (thread = lane kj of key ki's 8-lane dot product)
-        const int kj = t & 7;
-        const int rounds = (n + KPR - 1) / KPR;
-        for (int r = 0; r < rounds; ++r) {
-            const int i = (t >> 3) + KPR * r;
-            float acc8 = 0.0f;
-            if (i < n) {
-                if (i < ncached) {
-                    const int8_t* kr = kraw + i * D;
-                    // at most two scale groups per row (checked by the launchers)
-#pragma unroll
-                    for (int d = kj; d < D; d += 8)
-                        acc8 = fmaf(qs[d], __fmul_rn((float)kr[d], ksc[i * 2 + (d >= a.qgs ? 1 : 0)]), acc8);
-                } else {
-                    const __half* kr = a.Kn + (size_t)(c0 + i - a.cache_len) * a.kn_row;
-#pragma unroll
-                    for (int d = kj; d < D; d += 8) acc8 = fmaf(qs[d], h2f(kr[d]), acc8);
-                }
-            }
-            const int base = lane & ~7;
+        // phase 1: scores, one thread per key: the reference's 8 lane accumulators (lane m sums
+        // dims m, m + 8, ... in order) kept in registers, then the fixed fold
+        for (int i = t; i < n; i += NT) {
             float p[8];
 #pragma unroll
-            for (int m = 0; m < 8; ++m) p[m] = __shfl_sync(0xffffffffu, acc8, base + m);
+            for (int m = 0; m < 8; ++m) p[m] = 0.0f;
+            if (i < ncached) {
+                const int4* kr = reinterpret_cast<const int4*>(kraw + i * KR);
+                const float s0 = ksc[i * 2], s1 = ksc[i * 2 + 1];
+#pragma unroll 2
+                for (int c = 0; c < D / 16; ++c) {
+                    const int4 kv = kr[c];
+                    const int w4[4] = {kv.x, kv.y, kv.z, kv.w};
+                    const float4* q4 = reinterpret_cast<const float4*>(qs + 16 * c);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float4 qv = q4[j];
+                        const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int d = 16 * c + 4 * j + e;
+                            const int kb = (int)((unsigned)w4[j] << (24 - 8 * e)) >> 24;  // signed byte e of the word
+                            const float kf = __fmul_rn(i2f_small(kb), d >= a.qgs ? s1 : s0);
+                            p[(4 * j + e) & 7] = fmaf(qq[e], kf, p[(4 * j + e) & 7]);
+                        }
+                    }
+                }
+            } else {
+                const __half* kr = a.Kn + (size_t)(c0 + i - a.cache_len) * a.kn_row;
+                for (int d = 0; d < D; ++d) p[d & 7] = fmaf(qs[d], h2f(kr[d]), p[d & 7]);
+            }
             float s = __fmul_rn(fold8(p), a.scale);
-            if (i >= n || (a.causal && c0 + i > a.aq)) s = -INFINITY;
-            if (kj == 0 && i < CH) sc[i] = s;
+            if (a.causal && c0 + i > a.aq) s = -INFINITY;
+            sc[i] = s;
         }
-        bar();
         // phase 2: warp w owns block w of the chunk
         const int nb = (n + 31) / 32;
         if (warp < nb) {
@@ -190,7 +205,7 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
                     for (int j = 0; j < 32; ++j) {
                         const int i = i0 + j;
                         const float w = sc[i];
-                        const float v = __fmul_rn((float)vraw[i * D + t], vs_t[i * 2]);
+                        const float v = __fmul_rn(i2f_small(vraw[i * D + t]), vs_t[i * 2]);
                         const float nacc = fmaf(v, w, acc);
                         acc = (w == 0.0f) ? acc : nacc;
                     }

@@ -10,7 +10,7 @@
 //   1. attn_split_scores_kernel — one CTA per (sequence, query, kv head, 256 keys): scores
 //      of every q head of the group (8-lane dot products folded in the reference tree),
 //      block maxima, weights and in-order block sums, written to a scratch buffer;
-//   2. attn_split_chain_kernel — one CTA per (sequence, query, q head), one thread per dim:
+//   2. attn_split_chain_kernel — one CTA per (sequence, query, q head, 64 dims), thread = dim:
 //      the corrections of all blocks in parallel, then the in-order V recurrence over a
 //      4-stage cp.async ring of 128-key V chunks (the only serial part: one fmaf per key).
 // The result bits equal those of attn_exact_core (and of the reference) for every length.
@@ -77,9 +77,15 @@ template <int D>
 __host__ __device__ constexpr int s1_smem(int grp) {
     return kS1Keys * s1_row<D>() + kS1Keys * 2 * 4 + grp * D * 4 + grp * kS1Keys * 4;
 }
+// dims of one chain CTA: up to 64 (two warps), so a head's dims spread over D / 64 CTAs and a
+// single query keeps several SMs busy
 template <int D>
-__host__ __device__ constexpr int s2_stage_bytes() {  // V rows | weights | V scales [2][keys]
-    return kS2Keys * D + kS2Keys * 4 + kS2Keys * 2 * 4;
+__host__ __device__ constexpr int s2_dims() {
+    return D < 64 ? D : 64;
+}
+template <int D>
+__host__ __device__ constexpr int s2_stage_bytes() {  // V rows (this CTA's dims) | weights | V scales [2][keys]
+    return kS2Keys * s2_dims<D>() + kS2Keys * 4 + kS2Keys * 2 * 4;
 }
 
 // grid (B * S * Hkv, ceil(kv_seq_len / kS1Keys)), kS1Threads threads
@@ -184,14 +190,16 @@ __global__ void __launch_bounds__(kS1Threads) attn_split_scores_kernel(SplitArgs
     }
 }
 
-// grid B * S * Hq, D threads (thread t owns output dim t)
+// grid (B * S * Hq, D / DC), DC = s2_dims<D>() threads: thread t owns output dim blockIdx.y * DC + t
 template <int D>
-__global__ void __launch_bounds__(D) attn_split_chain_kernel(SplitArgs a) {
+__global__ void __launch_bounds__(s2_dims<D>()) attn_split_chain_kernel(SplitArgs a) {
     pdl_launch_dependents();
     pdl_wait();
     split_lengths(a);
     extern __shared__ __align__(16) uint8_t smem[];
     constexpr int SB = s2_stage_bytes<D>();
+    constexpr int DC = s2_dims<D>();
+    const int dim0 = blockIdx.y * DC;
     const long long item = blockIdx.x;
     const int h = (int)(item % a.Hq);
     const int qp = (int)((item / a.Hq) % a.S);
@@ -207,14 +215,14 @@ __global__ void __launch_bounds__(D) attn_split_chain_kernel(SplitArgs a) {
     float* bsm = bmx + a.nbw;
     float* corr = bsm + a.nbw;
     int* bz = reinterpret_cast<int*>(corr + a.nbw);
-    for (int j = t; j < nb; j += D) {
+    for (int j = t; j < nb; j += DC) {
         bmx[j] = a.bmx[item * a.nbw + j];
         bsm[j] = a.bsm[item * a.nbw + j];
         bz[j] = a.bz[item * a.nbw + j];
     }
     __syncthreads();
     // correction of block j: expf(max of the last non-empty block before j - max of j)
-    for (int j = t; j < nb; j += D) {
+    for (int j = t; j < nb; j += DC) {
         float pm = -INFINITY;
         for (int k = j - 1; k >= 0; --k) {
             if (bmx[k] > -INFINITY) {
@@ -232,34 +240,34 @@ __global__ void __launch_bounds__(D) attn_split_chain_kernel(SplitArgs a) {
     auto stage = [&](long long c) {
         uint8_t* st = smem + (int)(c % kS2Stages) * SB;
         int8_t* vraw = reinterpret_cast<int8_t*>(st);
-        float* wst = reinterpret_cast<float*>(st + kS2Keys * D);
+        float* wst = reinterpret_cast<float*>(st + kS2Keys * DC);
         float* vsc = wst + kS2Keys;
         const long long c0 = c * kS2Keys;
         const int n = (int)min((long long)kS2Keys, kv_end - c0);
         const int ncached = (int)max(0LL, min((long long)n, (long long)a.cache_len - c0));
-        for (int x = t; x < ncached * (D / 16); x += D) {
-            const int i = x / (D / 16), off = (x % (D / 16)) * 16;
-            cp_async16(vraw + i * D + off, Vc + (size_t)(c0 + i) * kv_row + off);
+        for (int x = t; x < ncached * (DC / 16); x += DC) {
+            const int i = x / (DC / 16), off = (x % (DC / 16)) * 16;
+            cp_async16(vraw + i * DC + off, Vc + (size_t)(c0 + i) * kv_row + dim0 + off);
         }
-        for (int x = t; x < ncached * nqg; x += D) {
+        for (int x = t; x < ncached * nqg; x += DC) {
             const int i = x / nqg, g = x % nqg;
             cp_async4(vsc + g * kS2Keys + i, vs + (size_t)(c0 + i) * sc_row + g);
         }
-        for (int x = t; x < n; x += D) cp_async4(wst + x, W + c0 + x);
+        for (int x = t; x < n; x += DC) cp_async4(wst + x, W + c0 + x);
         cp_async_commit();
     };
     for (int c = 0; c < kS2Stages - 1; ++c) {
         if (c < nch) stage(c);
         else cp_async_commit();
     }
-    const int vg = t / a.qgs;
+    const int vg = (dim0 + t) / a.qgs;
     float acc = 0.0f, run_sum = 0.0f;
     for (long long c = 0; c < nch; ++c) {
         cp_async_wait<kS2Stages - 2>();
         __syncthreads();
         const uint8_t* st = smem + (int)(c % kS2Stages) * SB;
         const int8_t* vraw = reinterpret_cast<const int8_t*>(st);
-        const float* wst = reinterpret_cast<const float*>(st + kS2Keys * D);
+        const float* wst = reinterpret_cast<const float*>(st + kS2Keys * DC);
         const float* vs_t = wst + kS2Keys + vg * kS2Keys;
         const long long c0 = c * kS2Keys;
         const int n = (int)min((long long)kS2Keys, kv_end - c0);
@@ -284,10 +292,10 @@ __global__ void __launch_bounds__(D) attn_split_chain_kernel(SplitArgs a) {
                 for (int j4 = 0; j4 < 8; ++j4) {
                     const float4 wq = w4[j4], sv = s4[j4];
                     const int i = i0 + 4 * j4;
-                    v[4 * j4 + 0] = __fmul_rn(i8_to_f(vraw[i * D + t]), sv.x);
-                    v[4 * j4 + 1] = __fmul_rn(i8_to_f(vraw[(i + 1) * D + t]), sv.y);
-                    v[4 * j4 + 2] = __fmul_rn(i8_to_f(vraw[(i + 2) * D + t]), sv.z);
-                    v[4 * j4 + 3] = __fmul_rn(i8_to_f(vraw[(i + 3) * D + t]), sv.w);
+                    v[4 * j4 + 0] = __fmul_rn(i8_to_f(vraw[i * DC + t]), sv.x);
+                    v[4 * j4 + 1] = __fmul_rn(i8_to_f(vraw[(i + 1) * DC + t]), sv.y);
+                    v[4 * j4 + 2] = __fmul_rn(i8_to_f(vraw[(i + 2) * DC + t]), sv.z);
+                    v[4 * j4 + 3] = __fmul_rn(i8_to_f(vraw[(i + 3) * DC + t]), sv.w);
                     w[4 * j4 + 0] = wq.x;
                     w[4 * j4 + 1] = wq.y;
                     w[4 * j4 + 2] = wq.z;
@@ -300,21 +308,21 @@ __global__ void __launch_bounds__(D) attn_split_chain_kernel(SplitArgs a) {
                 for (int j = 0; j < 32; ++j) {
                     const int i = i0 + j;
                     const float w = wst[i];
-                    const float v = __fmul_rn((float)vraw[i * D + t], vs_t[i]);
+                    const float v = __fmul_rn((float)vraw[i * DC + t], vs_t[i]);
                     const float nacc = fmaf(v, w, acc);
                     acc = (w == 0.0f) ? acc : nacc;
                 }
             } else {
                 for (int i = i0; i < ic; ++i) {
                     const float w = wst[i];
-                    const float v = __fmul_rn((float)vraw[i * D + t], vs_t[i]);
+                    const float v = __fmul_rn((float)vraw[i * DC + t], vs_t[i]);
                     const float nacc = fmaf(v, w, acc);
                     acc = (w == 0.0f) ? acc : nacc;
                 }
             }
             for (int i = ic; i < i1; ++i) {
                 const float w = wst[i];
-                const float v = h2f(Vn[(size_t)(c0 + i - a.cache_len) * kv_row + t]);
+                const float v = h2f(Vn[(size_t)(c0 + i - a.cache_len) * kv_row + dim0 + t]);
                 const float nacc = fmaf(v, w, acc);
                 acc = (w == 0.0f) ? acc : nacc;
             }
@@ -325,7 +333,7 @@ __global__ void __launch_bounds__(D) attn_split_chain_kernel(SplitArgs a) {
         else cp_async_commit();
     }
     cp_async_wait<0>();
-    a.o[item * D + t] = run_sum > 0.0f ? f2h(__fmul_rn(acc, __fdiv_rn(1.0f, run_sum))) : __float2half_rn(0.0f);
+    a.o[item * D + dim0 + t] = run_sum > 0.0f ? f2h(__fmul_rn(acc, __fdiv_rn(1.0f, run_sum))) : __float2half_rn(0.0f);
 }
 
 // Grow-only per-device scratch (old buffers stay allocated: kernels queued earlier on other
@@ -385,7 +393,7 @@ int launch_split(SplitArgs a, long long items, long long size_keys, int B, cudaS
     const long long nchunk = (size_keys + kS1Keys - 1) / kS1Keys;
     if (kv_items > 0x7FFFFFFFLL || nchunk > 65535 || items > 0x7FFFFFFFLL) return -1;
     launch_k(attn_split_scores_kernel<D>, dim3((unsigned)kv_items, (unsigned)nchunk), dim3(kS1Threads), sm1, st, a);
-    launch_k(attn_split_chain_kernel<D>, dim3((unsigned)items), dim3(D), sm2, st, a);
+    launch_k(attn_split_chain_kernel<D>, dim3((unsigned)items, D / s2_dims<D>()), dim3(s2_dims<D>()), sm2, st, a);
     return 0;
 }
 

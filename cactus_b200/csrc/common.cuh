@@ -36,6 +36,9 @@ unsigned* dev_error_ptr();
 
 // ---------------------------------------------------------------- fp16 helpers
 __device__ __forceinline__ float h2f(__half h) { return __half2float(h); }
+// Exact int -> fp32 for |x| < 2^22 without the conversion pipe: 1.5 * 2^23 + x holds x in the
+// low mantissa bits, so one integer add and one float subtract give (float)x exactly.
+__device__ __forceinline__ float i2f_small(int x) { return __fsub_rn(__int_as_float(0x4B400000 + x), 12582912.0f); }
 __device__ __forceinline__ __half f2h(float f) { return __float2half_rn(f); }
 __device__ __forceinline__ float h2f_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 __device__ __forceinline__ uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }

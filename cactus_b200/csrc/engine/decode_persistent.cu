@@ -196,8 +196,9 @@ __device__ __forceinline__ float rms_sumsq_lanemajor(const __half* xsT, int K) {
 
 // xs holds K fp16 activations (K % 8 == 0; K % 16 == 0 with a norm); optional RMSNorm with
 // weights `normw` (the load_vec call must have passed transposed = true), then the
-// activation quantisation (gemv.cuh prologues, same arithmetic) into act / *as.
-__device__ __forceinline__ void prologue(const Cs& m, int K, const __half* normw, float eps) {
+// activation quantisation (gemv.cuh prologues, same arithmetic) into act / *as. nw0 holds
+// normw's 16-byte chunk `threadIdx.x`, loaded early by the caller (see norm_chunk).
+__device__ __forceinline__ void prologue(const Cs& m, int K, const __half* normw, float eps, int4 nw0) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nch = K / 8;
     int4* x4 = reinterpret_cast<int4*>(m.xs);
@@ -214,7 +215,7 @@ __device__ __forceinline__ void prologue(const Cs& m, int K, const __half* normw
         const int4* w4 = reinterpret_cast<const int4*>(normw);
         for (int i = tid; i < nch; i += kPC) {
             int4 v = x4[i];
-            const int4 w = __ldg(w4 + i);
+            const int4 w = i == tid ? nw0 : __ldg(w4 + i);
             __half* h = reinterpret_cast<__half*>(&v);
             const __half* hw = reinterpret_cast<const __half*>(&w);
 #pragma unroll
@@ -254,6 +255,13 @@ __device__ __forceinline__ void prologue(const Cs& m, int K, const __half* normw
     cbar();
 }
 
+// The norm weights' 16-byte chunk of this thread, issued well before the prologue needs it so
+// its global-memory latency overlaps the preceding phase.
+__device__ __forceinline__ int4 norm_chunk(const __half* normw, int K) {
+    return (normw && (int)threadIdx.x < K / 8) ? __ldg(reinterpret_cast<const int4*>(normw) + threadIdx.x)
+                                               : make_int4(0, 0, 0, 0);
+}
+
 __device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
     if (v != v) return 0ull;
     unsigned u = __float_as_uint(v);
@@ -286,6 +294,9 @@ __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const C
         const int s = (int)(kslot % NS);
         const unsigned par = (kslot / NS) & 1;
         const int rows = min(spr, r1 - r);
+        // the residual row of this thread's output, read before the slot wait (the hidden
+        // state is stable since the last grid barrier)
+        const __half res = (epi == kEpiResid && tid < rows) ? __ldcg(out + r + tid) : __float2half_rn(0.0f);
         if (tid == 0) *m.flag = wait_abortable(&full[s], par, &a.sync->abort, 32) ? 1 : 0;
         cbar();
         if (!*m.flag) {
@@ -319,21 +330,22 @@ __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const C
             const int4* gp = reinterpret_cast<const int4*>(m.gsm + tid * gst);
             const float4* fp = reinterpret_cast<const float4*>(m.gsf + tid * gst);
             float run = 0.0f;
+            // group sums are below 2^22 in magnitude (G <= 128): exact integer -> float
             for (int c = 0; c < ng / 4; ++c) {
                 const int4 gv = gp[c];
                 const float4 fv = fp[c];
-                run = fmaf((float)gv.x, fv.x, run);
-                run = fmaf((float)gv.y, fv.y, run);
-                run = fmaf((float)gv.z, fv.z, run);
-                run = fmaf((float)gv.w, fv.w, run);
+                run = fmaf(i2f_small(gv.x), fv.x, run);
+                run = fmaf(i2f_small(gv.y), fv.y, run);
+                run = fmaf(i2f_small(gv.z), fv.z, run);
+                run = fmaf(i2f_small(gv.w), fv.w, run);
             }
-            for (int g = ng & ~3; g < ng; ++g) run = fmaf((float)m.gsm[tid * gst + g], m.gsf[tid * gst + g], run);
+            for (int g = ng & ~3; g < ng; ++g) run = fmaf(i2f_small(m.gsm[tid * gst + g]), m.gsf[tid * gst + g], run);
             const __half v = f2h(__fmul_rn(run, as));
             const int n = r + tid;
             if (epi == kEpiStore) {
                 out[n] = v;
             } else if (epi == kEpiResid) {
-                out[n] = __hadd(__ldcg(out + n), v);
+                out[n] = __hadd(res, v);
             } else if (epi == kEpiLm) {
                 out[n] = v;
                 const unsigned long long key = argmax_key(h2f(v), n);
@@ -358,17 +370,19 @@ __device__ __forceinline__ bool grid_sync(const PArgs& a, unsigned& nbar, int* f
         bool ok = !ld_volatile_u32(&a.sync->abort);
         if (ok) {
             // release: the block's writes (ordered before by the consumer barrier) become
-            // visible before the arrival; relaxed polling, one acquire fence at the end
+            // visible before the arrival
             red_release_gpu_add(&a.sync->bar, 1u);
             const unsigned target = nbar * gridDim.x;
             uint32_t i = 0;
-            while (ld_relaxed_gpu(&a.sync->bar) < target) {
+            // acquire loads: the observing load orders what follows, no separate fence (measured
+            // on B200 with 148 blocks: 1.40 us per barrier against 1.78 us for relaxed polling
+            // plus one acquire fence)
+            while (ld_acquire_gpu(&a.sync->bar) < target) {
                 if (++i > (1u << 22) || ((i & 63) == 0 && ld_volatile_u32(&a.sync->abort))) {
                     ok = false;
                     break;
                 }
             }
-            fence_acq_rel_gpu();
         }
         if (!ok) set_abort(a, kDevFlagTimeout);
         *flag = ok ? 1 : 0;
@@ -557,28 +571,30 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     embed_row(a, tok, m.xs);
     for (int l = 0; l < a.L; ++l) {
         const PLayer& ly = a.layers[l];
+        const int4 nw_in = norm_chunk(ly.in_norm, a.H), nw_post = norm_chunk(ly.post_norm, a.H);
         if (attn_block) attention_prefetch<D>(a, l, blockIdx.x, awork, cache_len, total_len);
         load_vec(m, l > 0 ? a.hidden : nullptr, a.H, true);
-        prologue(m, a.H, ly.in_norm, a.eps);
+        prologue(m, a.H, ly.in_norm, a.eps, nw_in);
         if (!gemv_job(a, 4 * l, kEpiStore, m, ring, full, empty, kslot, a.qkv, best)) return;
         if (!grid_sync(a, nbar, m.flag)) return;
         if (attn_block) attention_head<D>(a, l, blockIdx.x, awork, cache_len, total_len);
         if (!grid_sync(a, nbar, m.flag)) return;
         load_vec(m, a.attn, a.Hq * D, false);
-        prologue(m, a.Hq * D, nullptr, a.eps);
+        prologue(m, a.Hq * D, nullptr, a.eps, make_int4(0, 0, 0, 0));
         if (!gemv_job(a, 4 * l + 1, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
         if (!grid_sync(a, nbar, m.flag)) return;
         load_vec(m, a.hidden, a.H, true);
-        prologue(m, a.H, ly.post_norm, a.eps);
+        prologue(m, a.H, ly.post_norm, a.eps, nw_post);
         if (!gemv_job(a, 4 * l + 2, kEpiGlu, m, ring, full, empty, kslot, a.gated, best)) return;
         if (!grid_sync(a, nbar, m.flag)) return;
         load_vec(m, a.gated, a.F, false);
-        prologue(m, a.F, nullptr, a.eps);
+        prologue(m, a.F, nullptr, a.eps, make_int4(0, 0, 0, 0));
         if (!gemv_job(a, 4 * l + 3, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
         if (!grid_sync(a, nbar, m.flag)) return;
     }
+    const int4 nw_out = norm_chunk(a.out_norm, a.H);
     load_vec(m, a.hidden, a.H, true);
-    prologue(m, a.H, a.out_norm, a.eps);
+    prologue(m, a.H, a.out_norm, a.eps, nw_out);
     if (!gemv_job(a, 4 * a.L, kEpiLm, m, ring, full, empty, kslot, a.logits, best)) return;
     // block first-max, then the last block to finish picks the token
     for (int o = 16; o > 0; o >>= 1) {
