@@ -23,15 +23,6 @@ __device__ __forceinline__ float fold8(const float* a) {
                      __fadd_rn(__fadd_rn(a[2], a[6]), __fadd_rn(a[3], a[7])));
 }
 
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Row stride of the staged INT8 keys: 16 bytes of padding put the rows that eight consecutive
 // threads read with 16-byte loads into eight different bank groups.

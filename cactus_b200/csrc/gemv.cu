@@ -1,6 +1,8 @@
 // Host side of the grouped INT8/INT4 GEMV: shape checks, tile/stage selection and the
 // launch (optionally with programmatic dependent launch). The kernel is in gemv.cuh.
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "gemv.cuh"
 #include "ops.h"
@@ -10,6 +12,17 @@ namespace cb {
 namespace {
 
 using KernelFn = void (*)(GemvArgs);
+
+// CACTUS_B200_GEMV=rows selects the row-streaming kernel where its group-size condition holds.
+// The TMA tile kernel stays the default: on B200 both reach the same rate on a 165 MB weight
+// matrix and the tile kernel is faster on the few-MB projections of a decode step.
+bool gemv_rows_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("CACTUS_B200_GEMV");
+        return e && std::string(e) == "rows";
+    }();
+    return on;
+}
 
 template <int WF, int MT, int RPW, int PRO, int EPI>
 KernelFn fn() {
@@ -55,8 +68,33 @@ KernelFn pick_mt(int mt, int rpw, int ci) {
     }
 }
 
+template <int WF, int MT>
+KernelFn pick_rows_combo(int ci) {
+    switch (ci) {
+        case 0: return &qgemv_rows_kernel<WF, MT, kProPreq, kEpiStore>;
+        case 1: return &qgemv_rows_kernel<WF, MT, kProQuant, kEpiStore>;
+        case 2: return &qgemv_rows_kernel<WF, MT, kProQuant, kEpiResidual>;
+        case 3: return &qgemv_rows_kernel<WF, MT, kProRmsNormQuant, kEpiStore>;
+        case 4: return &qgemv_rows_kernel<WF, MT, kProRmsNormQuant, kEpiGluSilu>;
+        case 5: return &qgemv_rows_kernel<WF, MT, kProRmsNormQuant, kEpiGluGelu>;
+    }
+    return nullptr;
+}
+template <int WF>
+KernelFn pick_rows(int mt, int ci) {
+    switch (mt) {
+        case 1: return pick_rows_combo<WF, 1>(ci);
+        case 2: return pick_rows_combo<WF, 2>(ci);
+        case 4: return pick_rows_combo<WF, 4>(ci);
+        default: return pick_rows_combo<WF, 8>(ci);
+    }
+}
+
 std::mutex g_attr_mu;
 bool g_attr_set[2][9][5][kNumCombos] = {};
+// row-streaming variants: shared-memory attribute set, resident blocks per SM (0: unknown)
+bool g_rows_attr[2][9][kNumCombos] = {};
+int g_rows_per_sm[2][9][kNumCombos] = {};
 
 }  // namespace
 
@@ -100,6 +138,59 @@ void gemv_prepare() {
                                  cudaSuccess)
                         done = true;
                 }
+    for (int wf = 0; wf < 2; ++wf)
+        for (int mt : {1, 2, 4, 8})
+            for (int ci = 0; ci < kNumCombos; ++ci) {
+                bool& done = g_rows_attr[wf][mt][ci];
+                if (done) continue;
+                KernelFn f = wf ? pick_rows<1>(mt, ci) : pick_rows<0>(mt, ci);
+                if (f && cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) == cudaSuccess)
+                    done = true;
+            }
+}
+
+// Row-streaming launch (gemv.cuh: qgemv_rows_kernel); -2 when the shape does not qualify.
+static int launch_gemv_rows(const GemvCall& c, int mt, int ci, const GemvArgs& a, cudaStream_t st) {
+    if (!gemv_rows_ok(c.int4, c.G)) return -2;
+    const GemvRowsLayout L = gemv_rows_layout(c.int4, mt, c.pro, c.epi, c.K, c.G);
+    if (L.total > kSmemLimit) return -2;
+    KernelFn f = c.int4 ? pick_rows<1>(mt, ci) : pick_rows<0>(mt, ci);
+    if (!f) return -2;
+    int per_sm = 1;
+    {
+        std::lock_guard<std::mutex> lk(g_attr_mu);
+        if (!g_rows_attr[c.int4][mt][ci]) {
+            if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+                return -1;
+            g_rows_attr[c.int4][mt][ci] = true;
+        }
+        int& cached = g_rows_per_sm[c.int4][mt][ci];
+        if (cached == 0) {
+            int nb = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, f, kGemvThreads, 48 * 1024) != cudaSuccess)
+                nb = 1;
+            cached = nb < 1 ? 1 : nb;
+        }
+        per_sm = cached;
+    }
+    // resident blocks also limited by this shape's shared memory
+    const int by_smem = (228 * 1024) / (L.total + 1024);
+    if (by_smem < per_sm) per_sm = by_smem < 1 ? 1 : by_smem;
+    const int nrg = (c.N + L.RW - 1) / L.RW;
+    int grid = (nrg + kGemvWarps - 1) / kGemvWarps;
+    if (grid < kNumSMs) grid = nrg < kNumSMs ? nrg : kNumSMs;  // spread small outputs over the SMs
+    if (grid > per_sm * kNumSMs) grid = per_sm * kNumSMs;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (c.pdl || pdl_flag()) ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, f, a) == cudaSuccess ? 0 : -1;
 }
 
 int launch_gemv(const GemvCall& c, cudaStream_t st) {
@@ -148,6 +239,10 @@ int launch_gemv(const GemvCall& c, cudaStream_t st) {
     a.N = c.N;
     a.G = c.G;
     a.S = S;
+    if (gemv_rows_enabled()) {
+        const int r = launch_gemv_rows(c, mt, ci, a, st);
+        if (r != -2) return r;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kGemvThreads);

@@ -168,55 +168,17 @@ __device__ __forceinline__ int8_t quant_act(float v, float inv, bool vec) {
     return vec ? (int8_t)sat8(cvt_rne_sat(s)) : (int8_t)(int)roundf(s);
 }
 
-template <int WF, int MT, int RPW, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int S = a.S;
-    const GemvLayout L = gemv_layout(WF, MT, RPW, S, PRO, a.K, a.G);
+// Activation prologue of both GEMV kernels: the M rows of x (or the pre-quantised rows) into
+// `act` (int8, [MT][K]; INT4 weights: each 8-element block permuted so that dp4a pairs the even
+// and the odd k with the low and the high nibbles), the per-row scales into `as`, and for INT4
+// the per-group activation sums into `asum`. `xs` holds MT * K halves, `red` 72 floats (the
+// per-warp maxima and the sums of squares). Ends with a block barrier.
+template <int WF, int MT, int PRO>
+__device__ __forceinline__ void gemv_prologue(const GemvArgs& a, int8_t* act, int* asum, float* as, __half* xs,
+                                              float* red) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = a.K, N = a.N, G = a.G, M = a.M;
-    const int R = L.R, ng = L.ng;
-    const int ntiles = (N + R - 1) / R;
-
-    int8_t* act = reinterpret_cast<int8_t*>(smem + L.off_act);
-    int* asum = reinterpret_cast<int*>(smem + L.off_asum);
-    float* as = reinterpret_cast<float*>(smem + L.off_as);
-    int* s_abort = reinterpret_cast<int*>(smem + L.off_as + align_up(MT * 4, 16));
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.off_bar);
-    int* gsbuf = reinterpret_cast<int*>(smem + L.off_gs) + warp * L.pairs * L.gpj;
-    uint16_t* outt = reinterpret_cast<uint16_t*>(smem + L.off_out);
-
-    const uint8_t* wbase = reinterpret_cast<const uint8_t*>(a.w);
-    auto issue = [&](int t, int s) {
-        uint8_t* st = smem + L.off_stage + s * L.stage_bytes;
-        const int rows = min(R, N - t * R);
-        const unsigned wb = (unsigned)(rows * L.wrow);
-        const unsigned sb_all = (unsigned)(rows * ng * 2);
-        const unsigned sb = sb_all & ~15u;
-        mbar_arrive_expect_tx(&bar[s], wb + sb);
-        tma_load_1d(st, wbase + (size_t)t * R * L.wrow, wb, &bar[s]);
-        const uint16_t* sc = reinterpret_cast<const uint16_t*>(a.ws) + (size_t)t * R * ng;
-        if (sb) tma_load_1d(st + L.stage_w, sc, sb, &bar[s]);
-        for (unsigned i = sb / 2; i < sb_all / 2; ++i)  // sub-16-byte remainder of a partial tile
-            reinterpret_cast<uint16_t*>(st + L.stage_w)[i] = sc[i];
-    };
-
-    if (tid == 0) {
-        *s_abort = 0;
-        for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0)
-        for (int s = 0; s < S; ++s) {
-            const int t = blockIdx.x + s * gridDim.x;
-            if (t < ntiles) issue(t, s);
-        }
-    // Weights are constant: their copies above may overlap the previous kernel.
-    pdl_launch_dependents();
-    pdl_wait();
-
-    // ---------------------------------------------------------- prologue: activations -> smem int8
+    const int K = a.K, G = a.G, M = a.M;
+    const int ng = K / G;
     if constexpr (PRO == (int)Pro::PREQ) {
         for (int i = tid; i < M * K; i += kGemvThreads) {
             const int m = i / K, k = i % K;
@@ -234,8 +196,6 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
         // Latency-oriented: one global round trip stages the M rows, warp m reduces row m's
         // sum of squares, then one pass normalises + takes per-warp maxima and one pass
         // quantises (3 block barriers for RMSNorm, 2 otherwise).
-        __half* xs = reinterpret_cast<__half*>(smem + L.off_xs);
-        float* red = reinterpret_cast<float*>(smem + L.off_gs);  // [8][8] maxima + [8] sums of squares
         const int vec_end = (K / 8) * 8;
         if ((K & 7) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0) {
             const int4* src = reinterpret_cast<const int4*>(a.x);
@@ -306,6 +266,60 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
         __syncthreads();
     }
 
+}
+
+template <int WF, int MT, int RPW, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int S = a.S;
+    const GemvLayout L = gemv_layout(WF, MT, RPW, S, PRO, a.K, a.G);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = a.K, N = a.N, G = a.G, M = a.M;
+    const int R = L.R, ng = L.ng;
+    const int ntiles = (N + R - 1) / R;
+
+    int8_t* act = reinterpret_cast<int8_t*>(smem + L.off_act);
+    int* asum = reinterpret_cast<int*>(smem + L.off_asum);
+    float* as = reinterpret_cast<float*>(smem + L.off_as);
+    int* s_abort = reinterpret_cast<int*>(smem + L.off_as + align_up(MT * 4, 16));
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.off_bar);
+    int* gsbuf = reinterpret_cast<int*>(smem + L.off_gs) + warp * L.pairs * L.gpj;
+    uint16_t* outt = reinterpret_cast<uint16_t*>(smem + L.off_out);
+
+    const uint8_t* wbase = reinterpret_cast<const uint8_t*>(a.w);
+    auto issue = [&](int t, int s) {
+        uint8_t* st = smem + L.off_stage + s * L.stage_bytes;
+        const int rows = min(R, N - t * R);
+        const unsigned wb = (unsigned)(rows * L.wrow);
+        const unsigned sb_all = (unsigned)(rows * ng * 2);
+        const unsigned sb = sb_all & ~15u;
+        mbar_arrive_expect_tx(&bar[s], wb + sb);
+        tma_load_1d(st, wbase + (size_t)t * R * L.wrow, wb, &bar[s]);
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(a.ws) + (size_t)t * R * ng;
+        if (sb) tma_load_1d(st + L.stage_w, sc, sb, &bar[s]);
+        for (unsigned i = sb / 2; i < sb_all / 2; ++i)  // sub-16-byte remainder of a partial tile
+            reinterpret_cast<uint16_t*>(st + L.stage_w)[i] = sc[i];
+    };
+
+    if (tid == 0) {
+        *s_abort = 0;
+        for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0)
+        for (int s = 0; s < S; ++s) {
+            const int t = blockIdx.x + s * gridDim.x;
+            if (t < ntiles) issue(t, s);
+        }
+    // Weights are constant: their copies above may overlap the previous kernel.
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // ---------------------------------------------------------- prologue: activations -> smem int8
+    gemv_prologue<WF, MT, PRO>(a, act, asum, as, reinterpret_cast<__half*>(smem + L.off_xs),
+                               reinterpret_cast<float*>(smem + L.off_gs));
+
     // ---------------------------------------------------------- main loop over tiles
     // Per tile and per slice of 32 groups: (1) warps form the exact int32 group sums of their
     // rows (lanes split a row's 16-byte chunks, lanes of one group are folded by shuffles)
@@ -324,12 +338,16 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int s = it % S;
         const unsigned par = (unsigned)((it / S) & 1);
-        if (!mbar_wait_bounded(&bar[s], par)) {
+        // one thread polls the stage (a block of spinning threads takes issue slots from the
+        // co-resident block); after the barrier every thread checks the completed phase once,
+        // which orders its reads of the copied bytes
+        if (tid == 0 && !mbar_wait_bounded(&bar[s], par)) {
             report_dev_error(kDevTmaTimeout);
             atomicExch(s_abort, 1);
         }
         __syncthreads();
         if (*s_abort) return;  // uniform across the block
+        mbar_wait_bounded(&bar[s], par);
         const uint8_t* st = smem + L.off_stage + s * L.stage_bytes;
         const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + L.stage_w);
         uint16_t* ob = outt + (it & 1) * R * MT;
@@ -387,8 +405,21 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
                 const int gcount = min(32, ng - sl * 32);
                 const int* gp = gsm + tid * 33;
                 const uint16_t* sp = sc + pr * ng + sl * 32;
+                if ((ng & 7) == 0 && gcount == 32) {
+                    // a row's scales are contiguous: 16-byte loads (one-at-a-time 2-byte loads
+                    // across rows ng * 2 bytes apart hit the same banks)
+                    const int4* sp4 = reinterpret_cast<const int4*>(sp);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int4 sv = sp4[q];
+                        const uint16_t* s8 = reinterpret_cast<const uint16_t*>(&sv);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) run = fmaf((float)gp[q * 8 + e], h2f_bits(s8[e]), run);
+                    }
+                } else {
 #pragma unroll 8
-                for (int gl = 0; gl < gcount; ++gl) run = fmaf((float)gp[gl], h2f_bits(sp[gl]), run);
+                    for (int gl = 0; gl < gcount; ++gl) run = fmaf((float)gp[gl], h2f_bits(sp[gl]), run);
+                }
             }
             __syncthreads();
         }
@@ -418,6 +449,214 @@ __global__ void __launch_bounds__(kGemvThreads) qgemv_kernel(GemvArgs a) {
             }
         }
     }
+}
+
+// ------------------------------------------------------------------ row-streaming variant
+// Same arithmetic, another data path, for group sizes whose 16-byte weight chunks per group
+// (cpg = G/16 for INT8, G/32 for INT4) divide 32. After the shared prologue every warp works
+// alone on its own row groups (RW consecutive rows): a per-warp ring of kRowsStages shared-
+// memory stages is filled with cp.async (8 (row, pass) items of 32 lanes x 16 bytes = 4 KB
+// per stage, plus the slice's group scales), so every warp keeps 12 KB of weights in flight
+// while it forms the exact group sums with dp4a and a shuffle fold over the cpg lanes of a
+// group; lanes (row, m) of the same warp then continue the fp32 chains. No block barrier
+// after the prologue: warps never wait for one another.
+constexpr int kRowsItems = 8;   // (row, pass) items per stage: 8 x 32 lanes x 16 bytes
+constexpr int kRowsStages = 4;
+
+struct GemvRowsLayout {
+    int RW, stage_bytes, warp_bytes, off_act, off_asum, off_as, off_xs, off_red, off_warps, total;
+};
+
+__host__ __device__ inline int gemv_rows_per_warp(int wf, int MT, int G, int epi) {
+    const int cpg = wf == 0 ? G / 16 : G / 32;
+    int rw = kRowsItems / cpg;
+    if (rw > 8) rw = 8;
+    while (rw > 1 && rw * MT > 32) rw >>= 1;  // one chain lane per (row, activation row)
+    if (rw < 1) rw = 1;
+    if ((epi == (int)Epi::GLU_SILU || epi == (int)Epi::GLU_GELU) && rw < 2) rw = 2;
+    return rw;
+}
+
+__host__ __device__ inline GemvRowsLayout gemv_rows_layout(int wf, int MT, int pro, int epi, int K, int G) {
+    GemvRowsLayout L;
+    L.RW = gemv_rows_per_warp(wf, MT, G, epi);
+    const int ng = K / G;
+    L.stage_bytes = kRowsItems * 512 + L.RW * 64;  // weights | RW rows x 32 fp16 scales
+    L.warp_bytes = kRowsStages * L.stage_bytes + align_up(L.RW * MT * 33 * 4, 16);
+    int off = 0;
+    L.off_act = off;   off += align_up(MT * K, 128);
+    L.off_asum = off;  off += align_up(MT * ng * 4, 128);
+    L.off_as = off;    off += 128;
+    L.off_xs = off;    off += (pro != 0) ? align_up(MT * K * 2, 128) : 0;
+    L.off_red = off;   off += 128 * 4;
+    L.off_warps = off; off += kGemvWarps * L.warp_bytes;
+    L.total = align_up(off, 128);
+    return L;
+}
+
+__host__ __device__ inline bool gemv_rows_ok(int wf, int G) {
+    const int cpg = wf == 0 ? G / 16 : G / 32;
+    return cpg >= 1 && cpg <= 32 && (32 % cpg) == 0;
+}
+
+template <int WF, int MT, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) qgemv_rows_kernel(GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvRowsLayout L = gemv_rows_layout(WF, MT, PRO, EPI, a.K, a.G);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = a.K, N = a.N, G = a.G, M = a.M;
+    const int ng = K / G, RW = L.RW;
+    const int cpg = WF == 0 ? G / 16 : G / 32;     // 16-byte weight chunks per group (divides 32)
+    const int chunks = WF == 0 ? K / 16 : K / 32;  // 16-byte weight chunks per row
+    const int wrow = WF == 0 ? K : K / 2;
+    const int nslice = (ng + 31) / 32;
+    const int items = RW * cpg;                        // (row, pass) items of one slice
+    const int nbps = (items + kRowsItems - 1) / kRowsItems;  // stages per slice
+    const int NB = nslice * nbps;                      // stages per row group
+    const bool vec_s = (ng & 7) == 0;                  // scales move as 16-byte chunks
+    const int nwarps = gridDim.x * kGemvWarps;
+    const int first_rg = warp * gridDim.x + blockIdx.x;  // consecutive row groups on different SMs
+    const int nrg = (N + RW - 1) / RW;
+    int8_t* act = reinterpret_cast<int8_t*>(smem + L.off_act);
+    int* asum = reinterpret_cast<int*>(smem + L.off_asum);
+    float* as = reinterpret_cast<float*>(smem + L.off_as);
+    uint8_t* wsm = smem + L.off_warps + warp * L.warp_bytes;
+    int* gs = reinterpret_cast<int*>(wsm + kRowsStages * L.stage_bytes);
+    const uint8_t* wbase = reinterpret_cast<const uint8_t*>(a.w);
+    const uint16_t* sbase = reinterpret_cast<const uint16_t*>(a.ws);
+
+    // stage j of this warp: row group first_rg + (j / NB) * nwarps, slice, batch
+    auto issue = [&](int j) {
+        const int k = j / NB, rem = j % NB, sl = rem / nbps, b = rem % nbps;
+        const int rg = first_rg + k * nwarps;
+        if (rg < nrg) {
+            uint8_t* st = wsm + (j % kRowsStages) * L.stage_bytes;
+            const int row0 = rg * RW;
+#pragma unroll
+            for (int q = 0; q < kRowsItems; ++q) {
+                const int it = b * kRowsItems + q;
+                const int r = it / cpg, p = it % cpg;
+                const int c = (sl * cpg + p) * 32 + lane;
+                if (it < items && row0 + r < N && c < chunks)
+                    cp_async16(st + q * 512 + lane * 16, wbase + (size_t)(row0 + r) * wrow + (size_t)c * 16);
+            }
+            if (b == 0 && vec_s && lane < RW * 4 && sl * 32 + 32 <= ng) {
+                const int r = lane >> 2, qq = lane & 3;
+                if (row0 + r < N)
+                    cp_async16(st + kRowsItems * 512 + r * 64 + qq * 16, sbase + (size_t)(row0 + r) * ng + sl * 32 + qq * 8);
+            }
+        }
+        cp_async_commit();  // possibly empty: keeps the group count uniform
+    };
+
+    // weights do not depend on the previous kernel: the first stages stream while it finishes
+    for (int j = 0; j < kRowsStages - 1; ++j) issue(j);
+    pdl_launch_dependents();
+    pdl_wait();
+    gemv_prologue<WF, MT, PRO>(a, act, asum, as, reinterpret_cast<__half*>(smem + L.off_xs),
+                               reinterpret_cast<float*>(smem + L.off_red));
+
+    const int cr = lane / MT, cm = lane % MT;  // chain lane (row cr of the group, activation row cm)
+    const bool chain_lane = lane < RW * MT && cm < M;
+    float run = 0.0f;
+    int4 sv[4];
+    for (int j = 0;; ++j) {
+        const int k = j / NB, rem = j % NB, sl = rem / nbps, b = rem % nbps;
+        const int rg = first_rg + k * nwarps;
+        if (rg >= nrg) break;
+        cp_async_wait<kRowsStages - 2>();
+        __syncwarp();
+        issue(j + kRowsStages - 1);  // into the stage consumed by the previous iteration
+        const uint8_t* st = wsm + (j % kRowsStages) * L.stage_bytes;
+        const int row0 = rg * RW;
+        const int gcount = min(32, ng - sl * 32);
+        const int crow = row0 + cr;
+        const bool crow_ok = chain_lane && crow < N;
+        const bool vs_slice = vec_s && gcount == 32;
+        if (b == 0 && crow_ok && vs_slice) {
+            const int4* sp = reinterpret_cast<const int4*>(st + kRowsItems * 512 + cr * 64);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) sv[q] = sp[q];
+        }
+#pragma unroll
+        for (int q = 0; q < kRowsItems; ++q) {
+            const int it = b * kRowsItems + q;
+            if (it >= items) break;  // uniform across the warp
+            const int r = it / cpg, p = it % cpg;
+            const int c = (sl * cpg + p) * 32 + lane;
+            const bool cval = c < chunks;
+            const int gl = (p * 32 + lane) / cpg;  // group within the slice
+            const int4 wv = *reinterpret_cast<const int4*>(st + q * 512 + lane * 16);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                int acc = 0;
+                if (cval && m < M) {
+                    if constexpr (WF == 0) {
+                        const int4 av = *reinterpret_cast<const int4*>(act + m * K + c * 16);
+                        acc = dp4a_ss(av.x, wv.x, acc);
+                        acc = dp4a_ss(av.y, wv.y, acc);
+                        acc = dp4a_ss(av.z, wv.z, acc);
+                        acc = dp4a_ss(av.w, wv.w, acc);
+                    } else {
+                        const int4 a0 = *reinterpret_cast<const int4*>(act + m * K + c * 32);
+                        const int4 a1 = *reinterpret_cast<const int4*>(act + m * K + c * 32 + 16);
+                        const unsigned ww[4] = {(unsigned)wv.x, (unsigned)wv.y, (unsigned)wv.z, (unsigned)wv.w};
+                        const int ae[4] = {a0.x, a0.z, a1.x, a1.z};
+                        const int ao[4] = {a0.y, a0.w, a1.y, a1.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const unsigned lo = (ww[e] & 0x0F0F0F0Fu) ^ 0x08080808u;
+                            const unsigned hi = ((ww[e] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+                            acc = dp4a_su(ae[e], lo, acc);
+                            acc = dp4a_su(ao[e], hi, acc);
+                        }
+                    }
+                }
+                for (int o = 1; o < cpg; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if ((lane % cpg) == 0 && cval) {
+                    if constexpr (WF == 1) acc -= 8 * asum[m * ng + sl * 32 + gl];
+                    gs[(r * MT + m) * 33 + gl] = acc;
+                }
+            }
+        }
+        if (b == nbps - 1) {  // slice complete: continue the chains over its groups
+            __syncwarp();
+            if (crow_ok) {
+                const int* gp = gs + lane * 33;  // lane == cr * MT + cm
+                if (vs_slice) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint16_t* s8 = reinterpret_cast<const uint16_t*>(&sv[q]);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) run = fmaf((float)gp[q * 8 + e], h2f_bits(s8[e]), run);
+                    }
+                } else {
+                    const uint16_t* sp = sbase + (size_t)crow * ng + sl * 32;
+                    for (int g = 0; g < gcount; ++g) run = fmaf((float)gp[g], h2f_bits(__ldg(sp + g)), run);
+                }
+            }
+            if (sl == nslice - 1) {  // row group complete: chain lanes hold C[cm, crow]
+                const __half v = __float2half_rn(__fmul_rn(run, as[cm < M ? cm : 0]));
+                if constexpr (EPI == (int)Epi::STORE || EPI == (int)Epi::RESIDUAL) {
+                    if (crow_ok) {
+                        __half o = v;
+                        if constexpr (EPI == (int)Epi::RESIDUAL) o = __hadd(a.resid[(size_t)cm * N + crow], v);
+                        a.out[(size_t)cm * N + crow] = o;
+                    }
+                } else {
+                    // rows come in (gate, up) pairs: RW is even and row groups start at even rows
+                    const __half up = __shfl_down_sync(0xffffffffu, v, MT);
+                    if (crow_ok && (cr & 1) == 0 && crow + 1 < N) {
+                        const __half g = (EPI == (int)Epi::GLU_SILU) ? ref_silu(v) : ref_gelu(v);
+                        a.out[(size_t)cm * (N / 2) + crow / 2] = __hmul(g, up);
+                    }
+                }
+                run = 0.0f;
+            }
+        }
+        __syncwarp();  // the stage and the group sums are free for the next iteration
+    }
+    cp_async_wait<0>();
 }
 
 }  // namespace cb

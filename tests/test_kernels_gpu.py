@@ -183,6 +183,17 @@ def test_matmul_tcgen05_path_bit_exact():
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
 
+def test_gemv_row_streaming_path_bit_exact():
+    """The row-streaming GEMV (opt-in: CACTUS_B200_GEMV=rows, read once per process) on every
+    GEMV parity case above (M <= 15: pre-quantised, fused quantisation, config 1, Llama K=8192),
+    run in a child pytest process."""
+    env = dict(os.environ, CACTUS_B200_GEMV="rows")
+    r = subprocess.run([sys.executable, "-m", "pytest", os.path.abspath(__file__), "-q", "-m", "gpu", "-p",
+                        "no:cacheprovider", "-k", "matmul_prequantized or config1 or llama_down"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
+
 # L_ >= 512: the key-split kernels (attention_split.cu); below: one CTA per query
 @pytest.mark.parametrize("B,S,L_,Hq,Hkv,D", [(1, 1, 127, 16, 8, 128), (1, 1, 1024, 32, 8, 64),
                                              (1, 1, 4096, 4, 1, 256), (1, 4, 60, 16, 8, 128),
