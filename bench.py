@@ -307,9 +307,11 @@ def run_config1(args):
 
 
 def run_config5(args):
-    """Config 5 (decode half): INT8-cache attention, 16 q / 8 kv heads, D=128, one query per
-    sequence, L in {512, 4096, 32768} cached keys, B in {1, 8, 64}, through
-    cactus_cuda_attention_hybrid_int8_fp16. L2 is flushed (a 256 MB write) before each timed call."""
+    """Config 5: INT8-cache attention, 16 q / 8 kv heads, D=128, through
+    cactus_cuda_attention_hybrid_int8_fp16. Decode: one query per sequence, L in {512, 4096,
+    32768} cached keys, B in {1, 8, 64}. Prefill: 512 causal queries after L cached keys (the
+    (L, B) cases whose run stays within seconds). L2 is flushed (a 256 MB write) before each
+    timed call."""
     import torch
     import cactus_b200 as cb
     L = cb.lib()
@@ -354,6 +356,45 @@ def run_config5(args):
                               "achieved_gbs": nbytes / (ms / 1e3) / 1e9, "frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / hbm,
                               "peak_source": src, "l2": "flushed before each call"}), flush=True)
             del kc, vc
+    # prefill half: 512 causal queries appended after the L cached keys (positions L..L+511),
+    # new keys/values fp16; flops = B * 16 * 4 * 128 * (512 * L + 131328) (QK^T and PV)
+    _, bf16, _ = _peaks()
+    S = 512
+    for Lc, B in ((512, 1), (512, 8), (512, 64), (4096, 1), (4096, 8), (32768, 1)):
+        kc = torch.randint(-127, 128, (B, Lc, Hkv, D), dtype=torch.int8, device="cuda", generator=g)
+        vc = torch.randint(-127, 128, (B, Lc, Hkv, D), dtype=torch.int8, device="cuda", generator=g)
+        ks = torch.rand((Lc, Hkv, 1), device="cuda", generator=g) * 0.02
+        vs = torch.rand((Lc, Hkv, 1), device="cuda", generator=g) * 0.02
+        q = torch.randn((B, S, Hq, D), device="cuda", generator=g).half()
+        kn = torch.randn((B, S, Hkv, D), device="cuda", generator=g).half()
+        vn = torch.randn((B, S, Hkv, D), device="cuda", generator=g).half()
+        o = torch.empty_like(q)
+        st = torch.cuda.current_stream().cuda_stream
+
+        def call():
+            cb.check(L.cactus_cuda_attention_hybrid_int8_fp16(
+                q.data_ptr(), kc.data_ptr(), vc.data_ptr(), ks.data_ptr(), vs.data_ptr(), kn.data_ptr(),
+                vn.data_ptr(), o.data_ptr(), B, S, Lc, S, Hq, Hkv, D, 1.0 / D ** 0.5, Lc, 1, 128, st),
+                "attention_hybrid prefill")
+        call()
+        times = []
+        for _ in range(max(args.steps, 3)):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            call()
+            e1.record()
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = sorted(times)[len(times) // 2]
+        flops = B * Hq * 4.0 * D * (S * Lc + S * (S + 1) / 2)
+        print(json.dumps({"config": 5, "workload": f"prefill attention INT8 cache L={Lc} + {S} causal queries B={B} "
+                                                   f"(16/8 heads, D=128)",
+                          "ms": ms, "flops": flops, "tflops": flops / (ms / 1e3) / 1e12,
+                          "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / bf16, "peak_source": src,
+                          "note": "fp32 FMA arithmetic in the reference order (exact), not tensor-core math",
+                          "l2": "flushed before each call"}), flush=True)
+        del kc, vc, q, kn, vn, o
     return 0
 
 

@@ -34,7 +34,7 @@ __host__ __device__ constexpr int attn_krow() {
 // shared-memory footprint of attn_exact_core<D, CH> (a multiple of 16 bytes)
 template <int D, int CH>
 __host__ __device__ constexpr int attn_core_smem() {
-    return CH * attn_krow<D>() + CH * D + (CH * 2 * 2 + CH + 3 * (CH / 32)) * 4;
+    return CH * attn_krow<D>() + CH * D + (CH * 2 * 2 + CH + 4 * (CH / 32)) * 4;
 }
 
 struct SyncBlock {
@@ -99,6 +99,7 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
     float* bmx = sc + CH;                               // [CH/32] block maxima
     float* bsm = bmx + CH / 32;                         // [CH/32] block sums
     float* bcorr = bsm + CH / 32;                       // [CH/32] running-max corrections
+    int* bzf = reinterpret_cast<int*>(bcorr + CH / 32); // [CH/32] 1: the block has a zero weight
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const float* qs = a.qs;
     const int vg = t < D ? t / a.qgs : 0;  // V scale group of this thread's dim
@@ -161,9 +162,11 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
                 const float x = __shfl_sync(0xffffffffu, w, l);
                 if (l < bs) sum = __fadd_rn(sum, x);
             }
+            const unsigned zero = __ballot_sync(0xffffffffu, lane < bs && w == 0.0f);
             if (lane == 0) {
                 bmx[warp] = m;
                 bsm[warp] = sum;
+                bzf[warp] = zero ? 1 : 0;
             }
         }
         bar();
@@ -191,7 +194,33 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
                 const int i0 = blk * 32, i1 = min(n, i0 + 32);
                 const int ic = min(i1, max(i0, ncached));  // [i0, ic) cached, [ic, i1) new keys
                 const float* vs_t = vsc + vg;
-                if (ic - i0 == 32) {
+                if (ic - i0 == 32 && !bzf[blk]) {
+                    // no zero weight in the block: 16-byte weight / scale loads, the values of 16
+                    // keys dequantised ahead, then the plain fmaf chain (same operations)
+                    const float4* w4 = reinterpret_cast<const float4*>(sc + i0);
+                    const float4* s4 = reinterpret_cast<const float4*>(vsc + i0 * 2);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float v[16], w[16];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float4 q = w4[4 * h + j];
+                            w[4 * j] = q.x;
+                            w[4 * j + 1] = q.y;
+                            w[4 * j + 2] = q.z;
+                            w[4 * j + 3] = q.w;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 q = s4[8 * h + j];  // scales of keys 2j, 2j + 1: [key][2]
+                            const int i = i0 + 16 * h + 2 * j;
+                            v[2 * j] = __fmul_rn(i2f_small(vraw[i * D + t]), vg ? q.y : q.x);
+                            v[2 * j + 1] = __fmul_rn(i2f_small(vraw[(i + 1) * D + t]), vg ? q.w : q.z);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) acc = fmaf(v[j], w[j], acc);
+                    }
+                } else if (ic - i0 == 32) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const int i = i0 + j;

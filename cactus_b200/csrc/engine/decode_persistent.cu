@@ -362,17 +362,23 @@ __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const C
     return true;
 }
 
-// grid-wide barrier over the consumer warps of all blocks
-__device__ __forceinline__ bool grid_sync(const PArgs& a, unsigned& nbar, int* flag) {
+// Number of blocks that own rows of an N-row job (8-row units split evenly over P blocks).
+__host__ __device__ inline int blocks_with_rows(int N, int P) { return (N >> 3) < P ? (N >> 3) : P; }
+
+// grid-wide barrier over the consumer warps of all blocks. Only the `narrive` blocks that wrote
+// data in the phase before it arrive (`arrive`); every block waits. The target is cumulative
+// (`tgt`), the same in every block; a block that does not arrive still passes every barrier in
+// order, so later barriers that it does arrive at order its reads before any later overwrite.
+__device__ __forceinline__ bool grid_sync(const PArgs& a, unsigned& tgt, int* flag, bool arrive, int narrive) {
     cbar();
-    ++nbar;
+    tgt += (unsigned)narrive;
     if (threadIdx.x == 0) {
         bool ok = !ld_volatile_u32(&a.sync->abort);
         if (ok) {
             // release: the block's writes (ordered before by the consumer barrier) become
             // visible before the arrival
-            red_release_gpu_add(&a.sync->bar, 1u);
-            const unsigned target = nbar * gridDim.x;
+            if (arrive) red_release_gpu_add(&a.sync->bar, 1u);
+            const unsigned target = tgt;
             uint32_t i = 0;
             // acquire loads: the observing load orders what follows, no separate fence (measured
             // on B200 with 148 blocks: 1.40 us per barrier against 1.78 us for relaxed polling
@@ -566,7 +572,16 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     const uint32_t tok = __ldcg(a.tok_in);
     uint8_t* awork = work + a.attn_off;
     const bool attn_block = (int)blockIdx.x < a.Hq;
-    unsigned kslot = 0, nbar = 0;
+    unsigned kslot = 0, tgt = 0;
+    const int P = gridDim.x, c = blockIdx.x;
+    int rr0, rr1;
+    rows_of(a.H, c, P, rr0, rr1);
+    const bool rows_h = rr1 > rr0;                 // rows of O and down (N = H)
+    rows_of(a.QKVN, c, P, rr0, rr1);
+    const bool rows_qkv = rr1 > rr0;
+    rows_of(2 * a.F, c, P, rr0, rr1);
+    const bool rows_gu = rr1 > rr0;
+    const int n_qkv = blocks_with_rows(a.QKVN, P), n_h = blocks_with_rows(a.H, P), n_gu = blocks_with_rows(2 * a.F, P);
     unsigned long long best = 0ull;
     embed_row(a, tok, m.xs);
     for (int l = 0; l < a.L; ++l) {
@@ -576,21 +591,21 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
         load_vec(m, l > 0 ? a.hidden : nullptr, a.H, true);
         prologue(m, a.H, ly.in_norm, a.eps, nw_in);
         if (!gemv_job(a, 4 * l, kEpiStore, m, ring, full, empty, kslot, a.qkv, best)) return;
-        if (!grid_sync(a, nbar, m.flag)) return;
+        if (!grid_sync(a, tgt, m.flag, rows_qkv, n_qkv)) return;
         if (attn_block) attention_head<D>(a, l, blockIdx.x, awork, cache_len, total_len);
-        if (!grid_sync(a, nbar, m.flag)) return;
+        if (!grid_sync(a, tgt, m.flag, attn_block, a.Hq)) return;
         load_vec(m, a.attn, a.Hq * D, false);
         prologue(m, a.Hq * D, nullptr, a.eps, make_int4(0, 0, 0, 0));
         if (!gemv_job(a, 4 * l + 1, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
-        if (!grid_sync(a, nbar, m.flag)) return;
+        if (!grid_sync(a, tgt, m.flag, rows_h, n_h)) return;
         load_vec(m, a.hidden, a.H, true);
         prologue(m, a.H, ly.post_norm, a.eps, nw_post);
         if (!gemv_job(a, 4 * l + 2, kEpiGlu, m, ring, full, empty, kslot, a.gated, best)) return;
-        if (!grid_sync(a, nbar, m.flag)) return;
+        if (!grid_sync(a, tgt, m.flag, rows_gu, n_gu)) return;
         load_vec(m, a.gated, a.F, false);
         prologue(m, a.F, nullptr, a.eps, make_int4(0, 0, 0, 0));
         if (!gemv_job(a, 4 * l + 3, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
-        if (!grid_sync(a, nbar, m.flag)) return;
+        if (!grid_sync(a, tgt, m.flag, rows_h, n_h)) return;
     }
     const int4 nw_out = norm_chunk(a.out_norm, a.H);
     load_vec(m, a.hidden, a.H, true);
