@@ -147,6 +147,8 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
             if (a.causal && c0 + i > a.aq) s = -INFINITY;
             sc[i] = s;
         }
+        // no barrier: with CH <= NT key i is scored by thread i, and phase 2 reads key i in
+        // lane i % 32 of warp i / 32, i.e. in the same thread
         // phase 2: warp w owns block w of the chunk
         const int nb = (n + 31) / 32;
         if (warp < nb) {

@@ -587,10 +587,12 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     const int n_qkv = blocks_with_rows(a.QKVN, P), n_h = blocks_with_rows(a.H, P), n_gu = blocks_with_rows(2 * a.F, P);
     unsigned long long best = 0ull;
     embed_row(a, tok, m.xs);
+    // attention blocks stage layer 0's cached K/V rows (later layers: at the end of the layer
+    // before, off the critical path of the QKV phase)
+    if (attn_block) attention_prefetch<D>(a, 0, blockIdx.x, awork, cache_len, total_len);
     for (int l = 0; l < a.L; ++l) {
         const PLayer& ly = a.layers[l];
         const int4 nw_in = norm_chunk(ly.in_norm, a.H), nw_post = norm_chunk(ly.post_norm, a.H);
-        if (attn_block) attention_prefetch<D>(a, l, blockIdx.x, awork, cache_len, total_len);
         load_vec(m, l > 0 ? a.hidden : nullptr, a.H, true);
         prologue(m, a.H, ly.in_norm, a.eps, nw_in);
         if (!gemv_job(a, 4 * l, kEpiStore, m, ring, full, empty, kslot, a.qkv, best)) return;
@@ -608,6 +610,8 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
         load_vec(m, a.gated, a.F, false);
         prologue(m, a.F, nullptr, a.eps, make_int4(0, 0, 0, 0));
         if (!gemv_job(a, 4 * l + 3, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
+        // the next layer's cache rows are fixed for this token and the staging area is free
+        if (attn_block && l + 1 < a.L) attention_prefetch<D>(a, l + 1, blockIdx.x, awork, cache_len, total_len);
         if (!grid_sync(a, tgt, m.flag, rows_h, n_h)) return;
     }
     const int4 nw_out = norm_chunk(a.out_norm, a.H);
