@@ -7,7 +7,7 @@
 // The recurrence only chains the per-block (max, sum) pair and the per-dim accumulator;
 // scores, block maxima, weights and block sums of a block depend on that block alone. So a
 // chunk of CH keys is processed in phases:
-//   1. all scores in parallel (one thread per key keeps the reference's 8 lane accumulators),
+//   1. all scores in parallel (8-lane dot products in the reference lane order),
 //   2. per 32-key block (one warp each): max, weights expf(s - max), in-order block sum,
 //   3. per output dim (one thread each): walk the blocks in order applying the correction
 //      expf(run_max - block_max) and the in-order V FMAs — the same operation sequence, so
@@ -24,8 +24,8 @@ __device__ __forceinline__ float fold8(const float* a) {
 }
 
 
-// Row stride of the staged INT8 keys: 16 bytes of padding put the rows that eight consecutive
-// threads read with 16-byte loads into eight different bank groups.
+// Row stride of the staged INT8 keys (16 bytes of padding: consecutive keys start in
+// different banks).
 template <int D>
 __host__ __device__ constexpr int attn_krow() {
     return D + 16;
@@ -112,43 +112,37 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
         if (!(c0 == 0 && a.prestaged)) attn_stage_chunk<D, NT, CH>(a, smem, c0);
         cp_async_wait<0>();
         bar();
-        // phase 1: scores, one thread per key: the reference's 8 lane accumulators (lane m sums
-        // dims m, m + 8, ... in order) kept in registers, then the fixed fold
-        for (int i = t; i < n; i += NT) {
+        // phase 1: scores (thread = lane kj of key ki's 8-lane dot product: lane kj sums dims
+        // kj, kj + 8, ... in order, then the fixed fold of the 8 lanes)
+        constexpr int KPR = NT / 8;  // keys per scoring round
+        const int kj = t & 7;
+        const int rounds = (n + KPR - 1) / KPR;
+        for (int r = 0; r < rounds; ++r) {
+            const int i = (t >> 3) + KPR * r;
+            float acc8 = 0.0f;
+            if (i < n) {
+                if (i < ncached) {
+                    const int8_t* kr = kraw + i * KR;
+                    const float s0 = ksc[i * 2], s1 = ksc[i * 2 + 1];
+                    // at most two scale groups per row (checked by the launchers)
+#pragma unroll
+                    for (int d = kj; d < D; d += 8)
+                        acc8 = fmaf(qs[d], __fmul_rn(i2f_small(kr[d]), d >= a.qgs ? s1 : s0), acc8);
+                } else {
+                    const __half* kr = a.Kn + (size_t)(c0 + i - a.cache_len) * a.kn_row;
+#pragma unroll
+                    for (int d = kj; d < D; d += 8) acc8 = fmaf(qs[d], h2f(kr[d]), acc8);
+                }
+            }
+            const int base = lane & ~7;
             float p[8];
 #pragma unroll
-            for (int m = 0; m < 8; ++m) p[m] = 0.0f;
-            if (i < ncached) {
-                const int4* kr = reinterpret_cast<const int4*>(kraw + i * KR);
-                const float s0 = ksc[i * 2], s1 = ksc[i * 2 + 1];
-#pragma unroll 2
-                for (int c = 0; c < D / 16; ++c) {
-                    const int4 kv = kr[c];
-                    const int w4[4] = {kv.x, kv.y, kv.z, kv.w};
-                    const float4* q4 = reinterpret_cast<const float4*>(qs + 16 * c);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float4 qv = q4[j];
-                        const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int d = 16 * c + 4 * j + e;
-                            const int kb = (int)((unsigned)w4[j] << (24 - 8 * e)) >> 24;  // signed byte e of the word
-                            const float kf = __fmul_rn(i2f_small(kb), d >= a.qgs ? s1 : s0);
-                            p[(4 * j + e) & 7] = fmaf(qq[e], kf, p[(4 * j + e) & 7]);
-                        }
-                    }
-                }
-            } else {
-                const __half* kr = a.Kn + (size_t)(c0 + i - a.cache_len) * a.kn_row;
-                for (int d = 0; d < D; ++d) p[d & 7] = fmaf(qs[d], h2f(kr[d]), p[d & 7]);
-            }
+            for (int m = 0; m < 8; ++m) p[m] = __shfl_sync(0xffffffffu, acc8, base + m);
             float s = __fmul_rn(fold8(p), a.scale);
-            if (a.causal && c0 + i > a.aq) s = -INFINITY;
-            sc[i] = s;
+            if (i >= n || (a.causal && c0 + i > a.aq)) s = -INFINITY;
+            if (kj == 0 && i < CH) sc[i] = s;
         }
-        // no barrier: with CH <= NT key i is scored by thread i, and phase 2 reads key i in
-        // lane i % 32 of warp i / 32, i.e. in the same thread
+        bar();
         // phase 2: warp w owns block w of the chunk
         const int nb = (n + 31) / 32;
         if (warp < nb) {
