@@ -272,8 +272,54 @@ __global__ void __launch_bounds__(s2_dims<D>()) attn_split_chain_kernel(SplitArg
         const long long c0 = c * kS2Keys;
         const int n = (int)min((long long)kS2Keys, kv_end - c0);
         const int ncached = (int)max(0LL, min((long long)n, (long long)a.cache_len - c0));
-        for (int bl = 0; bl < (n + 31) / 32; ++bl) {
-            const int blk = (int)(c0 / 32) + bl;
+        const int blk0 = (int)(c0 / 32);
+        // full chunk of cached keys, every block non-empty and without a zero weight: straight-
+        // line code in which the values of block b + 1 are dequantised ahead of block b's fmaf
+        // chain, so the scheduler overlaps the two (the same operations per dim, in order)
+        bool fast = n == kS2Keys && ncached == n;
+#pragma unroll
+        for (int bl = 0; bl < kS2Keys / 32; ++bl) fast = fast && bmx[blk0 + bl] > -INFINITY && !bz[blk0 + bl];
+        if (fast) {
+            auto deq = [&](float (&v)[32], int i0) {
+                const float4* s4 = reinterpret_cast<const float4*>(vs_t + i0);
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 sv = s4[j4];
+                    const int i = i0 + 4 * j4;
+                    v[4 * j4 + 0] = __fmul_rn(i8_to_f(vraw[i * DC + t]), sv.x);
+                    v[4 * j4 + 1] = __fmul_rn(i8_to_f(vraw[(i + 1) * DC + t]), sv.y);
+                    v[4 * j4 + 2] = __fmul_rn(i8_to_f(vraw[(i + 2) * DC + t]), sv.z);
+                    v[4 * j4 + 3] = __fmul_rn(i8_to_f(vraw[(i + 3) * DC + t]), sv.w);
+                }
+            };
+            auto step = [&](const float (&v)[32], int bl) {
+                const float cr = corr[blk0 + bl];
+                run_sum = __fmul_rn(run_sum, cr);
+                acc = __fmul_rn(acc, cr);
+                const float4* w4 = reinterpret_cast<const float4*>(wst + bl * 32);
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 wq = w4[j4];
+                    acc = fmaf(v[4 * j4 + 0], wq.x, acc);
+                    acc = fmaf(v[4 * j4 + 1], wq.y, acc);
+                    acc = fmaf(v[4 * j4 + 2], wq.z, acc);
+                    acc = fmaf(v[4 * j4 + 3], wq.w, acc);
+                }
+                run_sum = __fadd_rn(run_sum, bsm[blk0 + bl]);
+            };
+            static_assert(kS2Keys == 128, "four 32-key blocks per chunk");
+            float va[32], vb[32];
+            deq(va, 0);
+            deq(vb, 32);
+            step(va, 0);
+            deq(va, 64);
+            step(vb, 1);
+            deq(vb, 96);
+            step(va, 2);
+            step(vb, 3);
+        }
+        for (int bl = 0; !fast && bl < (n + 31) / 32; ++bl) {
+            const int blk = blk0 + bl;
             if (bmx[blk] > -INFINITY) {
                 const float cr = corr[blk];
                 run_sum = __fmul_rn(run_sum, cr);
