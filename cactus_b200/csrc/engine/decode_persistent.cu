@@ -50,11 +50,13 @@ struct SyncConsumers {
 
 __host__ __device__ inline int a128(int v) { return (v + 127) / 128 * 128; }
 
-// rows of an [N, K] matrix owned by block c of P: 8-row units split evenly
+// rows of an [N, K] matrix owned by block c of P: 8-row units split evenly. 32-bit unsigned
+// arithmetic (persistent_plan checks (N / 8) * (P + 1) < 2^31): a 64-bit division is a long
+// software sequence, and this runs at the start of every projection.
 __host__ __device__ inline void rows_of(int N, int c, int P, int& r0, int& r1) {
-    const long long U = N >> 3;
-    r0 = (int)((U * c) / P) * 8;
-    r1 = (int)((U * (c + 1)) / P) * 8;
+    const unsigned U = (unsigned)N >> 3;
+    r0 = (int)((U * (unsigned)c) / (unsigned)P) * 8;
+    r1 = (int)((U * (unsigned)(c + 1)) / (unsigned)P) * 8;
 }
 
 struct JobW {
@@ -674,8 +676,10 @@ PPlan persistent_plan(PArgs& a, int num_sms, size_t smem_optin) {
         kmax = K > kmax ? K : kmax;
     }
     const int Ns[5] = {a.QKVN, a.H, 2 * a.F, a.H, a.V};
-    for (int N : Ns)
+    for (int N : Ns) {
         if (N % 8) return no("rows not a multiple of 8");
+        if ((long long)(N >> 3) * (num_sms + 1) >= (1LL << 31)) return no("too many rows for 32-bit row ranges");
+    }
     a.kmax = kmax;
     // A slot holds 48 rows at K = 1024, so a block's share of every projection of a Qwen3-0.6B
     // layer (QKV 24-32 rows, gate-up 40-48 rows, O / down 8 rows) is one slot: no block trails
