@@ -8,7 +8,8 @@
 // scores, block maxima, weights and block sums of a block depend on that block alone. So a
 // chunk of CH keys is processed in phases:
 //   1. all scores in parallel (8-lane dot products in the reference lane order),
-//   2. per 32-key block (one warp each): max, weights expf(s - max), in-order block sum,
+//   2. per 32-key block (one warp each): max, weights expf(s - max), in-order block sum and
+//      the block's correction (from the max of the last non-empty block before it),
 //   3. per output dim (one thread each): walk the blocks in order applying the correction
 //      expf(run_max - block_max) and the in-order V FMAs — the same operation sequence, so
 //      the result is bit-identical, with only the V chain left sequential.
@@ -34,7 +35,7 @@ __host__ __device__ constexpr int attn_krow() {
 // shared-memory footprint of attn_exact_core<D, CH> (a multiple of 16 bytes)
 template <int D, int CH>
 __host__ __device__ constexpr int attn_core_smem() {
-    return CH * attn_krow<D>() + CH * D + (CH * 2 * 2 + CH + 4 * (CH / 32)) * 4;
+    return CH * attn_krow<D>() + CH * D + (CH * 2 * 2 + 2 * CH + 4 * (CH / 32)) * 4;
 }
 
 struct SyncBlock {
@@ -95,8 +96,9 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
     int8_t* vraw = kraw + CH * KR;                      // [CH][D]
     float* ksc = reinterpret_cast<float*>(vraw + CH * D);  // [CH][2]
     float* vsc = ksc + CH * 2;                          // [CH][2]
-    float* sc = vsc + CH * 2;                           // [CH] scores, then weights
-    float* bmx = sc + CH;                               // [CH/32] block maxima
+    float* sc = vsc + CH * 2;                           // [CH] scores
+    float* sw = sc + CH;                                // [CH] weights
+    float* bmx = sw + CH;                               // [CH/32] block maxima
     float* bsm = bmx + CH / 32;                         // [CH/32] block sums
     float* bcorr = bsm + CH / 32;                       // [CH/32] running-max corrections
     int* bzf = reinterpret_cast<int*>(bcorr + CH / 32); // [CH/32] 1: the block has a zero weight
@@ -151,7 +153,20 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
             const float s = lane < bs ? sc[i] : -INFINITY;
             const float m = warp_max(s);
             const float w = (lane < bs && s != -INFINITY) ? expf_cr(__fsub_rn(s, m)) : 0.0f;
-            if (lane < bs) sc[i] = w;
+            if (lane < bs) sw[i] = w;
+            // the correction of this block, expf(running max before it - its max): the running
+            // max is the max of the last non-empty block before it in the chunk, else that of
+            // the earlier chunks; a maximum is exact in any order, so the warp recomputes it from
+            // the scores (blocks before the last one of a chunk are full)
+            float pm = run_max;
+            for (int j = warp - 1; j >= 0; --j) {
+                const float mj = warp_max(sc[j * 32 + lane]);
+                if (mj > -INFINITY) {
+                    pm = mj;
+                    break;
+                }
+            }
+            const float corr = expf_cr(__fsub_rn(pm, m));
             float sum = 0.0f;
 #pragma unroll
             for (int l = 0; l < 32; ++l) {
@@ -163,16 +178,8 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
                 bmx[warp] = m;
                 bsm[warp] = sum;
                 bzf[warp] = zero ? 1 : 0;
+                bcorr[warp] = corr;
             }
-        }
-        bar();
-        // the correction of block b, expf(running max before b - max of b), depends only on
-        // block maxima: computed for all blocks at once
-        if (t < nb) {
-            float pm = run_max;
-            for (int j = 0; j < t; ++j)
-                if (bmx[j] > -INFINITY) pm = bmx[j];
-            bcorr[t] = expf_cr(__fsub_rn(pm, bmx[t]));
         }
         bar();
         // phase 3: the reference's sequential recurrence, one output dim per thread
@@ -193,7 +200,7 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
                 if (ic - i0 == 32 && !bzf[blk]) {
                     // no zero weight in the block: 16-byte weight / scale loads, the values of 16
                     // keys dequantised ahead, then the plain fmaf chain (same operations)
-                    const float4* w4 = reinterpret_cast<const float4*>(sc + i0);
+                    const float4* w4 = reinterpret_cast<const float4*>(sw + i0);
                     const float4* s4 = reinterpret_cast<const float4*>(vsc + i0 * 2);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
@@ -220,21 +227,21 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const int i = i0 + j;
-                        const float w = sc[i];
+                        const float w = sw[i];
                         const float v = __fmul_rn(i2f_small(vraw[i * D + t]), vs_t[i * 2]);
                         const float nacc = fmaf(v, w, acc);
                         acc = (w == 0.0f) ? acc : nacc;
                     }
                 } else {
                     for (int i = i0; i < ic; ++i) {
-                        const float w = sc[i];
+                        const float w = sw[i];
                         const float v = __fmul_rn((float)vraw[i * D + t], vs_t[i * 2]);
                         const float nacc = fmaf(v, w, acc);
                         acc = (w == 0.0f) ? acc : nacc;
                     }
                 }
                 for (int i = ic; i < i1; ++i) {
-                    const float w = sc[i];
+                    const float w = sw[i];
                     const float v = h2f(a.Vn[(size_t)(c0 + i - a.cache_len) * a.kn_row + t]);
                     const float nacc = fmaf(v, w, acc);
                     acc = (w == 0.0f) ? acc : nacc;
