@@ -481,6 +481,10 @@ __device__ __forceinline__ void attention_head(const PArgs& a, int l, int h, uin
     float* qs = sm.qs;
     __half *hq = sm.hq, *hk = sm.hk, *hv = sm.hv, *qr = sm.qr, *kr = sm.kr;
     const PLayer& ly = a.layers[l];
+    // every layer pointer is read here, next to the q/k/v loads: the block barriers below are
+    // memory clobbers, so a read placed after one would add an L2 round trip to the phase
+    const AttnCoreArgs c = attn_args<D>(a, ly, h, cache_len, total_len, qs, kr, hv);
+    const bool rope = ly.ct != nullptr, qnorm = ly.q_norm != nullptr, knorm = ly.k_norm != nullptr;
     for (int d = tid; d < D; d += kPC) {
         hq[d] = __ldcg(a.qkv + (size_t)h * D + d);
         hk[d] = __ldcg(a.qkv + (size_t)(a.Hq + kvh) * D + d);
@@ -488,22 +492,22 @@ __device__ __forceinline__ void attention_head(const PArgs& a, int l, int h, uin
     }
     cp_async_wait<0>();  // the prefetched norm weights / RoPE rows / K/V of this thread
     cbar();
-    const __half* crow = ly.ct ? sm.crow : nullptr;
-    if (warp == 0) head_norm_rope_rows(hq, D, ly.q_norm ? sm.qn : nullptr, a.eps, crow, sm.srow, qr);
-    else if (warp == 1) head_norm_rope_rows(hk, D, ly.k_norm ? sm.kn : nullptr, a.eps, crow, sm.srow, kr);
+    const __half* crow = rope ? sm.crow : nullptr;
+    if (warp == 0) head_norm_rope_rows(hq, D, qnorm ? sm.qn : nullptr, a.eps, crow, sm.srow, qr);
+    else if (warp == 1) head_norm_rope_rows(hk, D, knorm ? sm.kn : nullptr, a.eps, crow, sm.srow, kr);
     cbar();
     for (int d = tid; d < D; d += kPC) qs[d] = h2f(qr[d]);
     // the first q head of each group appends the step's K/V to the cache at slot cache_len
+    // (c.Kc / c.Vc / c.ks / c.vs point at this kv head's row 0)
     if (h % grp == 0 && warp >= 2 && warp < 2 + 2 * nqg) {
         const int which = (warp - 2) / nqg, g = (warp - 2) % nqg;
         const int cnt = min(128, D - g * 128);
         const __half* src = (which ? hv : kr) + g * 128;
-        int8_t* dst = (which ? ly.vc : ly.kc) + ((size_t)cache_len * a.Hkv + kvh) * D + g * 128;
-        float* sdst = (which ? ly.vs : ly.ks) + ((size_t)cache_len * a.Hkv + kvh) * nqg + g;
+        int8_t* dst = const_cast<int8_t*>(which ? c.Vc : c.Kc) + (size_t)cache_len * c.kv_row + g * 128;
+        float* sdst = const_cast<float*>(which ? c.vs : c.ks) + (size_t)cache_len * c.sc_row + g;
         kv_quant_group_warp(src, cnt, dst, sdst);
     }
     cbar();
-    const AttnCoreArgs c = attn_args<D>(a, ly, h, cache_len, total_len, qs, kr, hv);
     const __half o = attn_exact_core<D, kPC, kACH>(c, work, SyncConsumers{});
     if (tid < D) a.attn[(size_t)h * D + tid] = o;
 }
