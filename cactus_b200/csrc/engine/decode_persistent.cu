@@ -598,9 +598,13 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     if (attn_block) attention_prefetch<D>(a, 0, blockIdx.x, awork, cache_len, total_len);
     for (int l = 0; l < a.L; ++l) {
         const PLayer& ly = a.layers[l];
-        const int4 nw_in = norm_chunk(ly.in_norm, a.H), nw_post = norm_chunk(ly.post_norm, a.H);
+        // norm pointers in registers: reads of `ly` after a block barrier (a memory clobber)
+        // would be repeated as L2 round trips
+        const __half* const in_norm = ly.in_norm;
+        const __half* const post_norm = ly.post_norm;
+        const int4 nw_in = norm_chunk(in_norm, a.H), nw_post = norm_chunk(post_norm, a.H);
         load_vec(m, l > 0 ? a.hidden : nullptr, a.H, true);
-        prologue(m, a.H, ly.in_norm, a.eps, nw_in);
+        prologue(m, a.H, in_norm, a.eps, nw_in);
         if (!gemv_job(a, 4 * l, kEpiStore, m, ring, full, empty, kslot, a.qkv, best)) return;
         if (!grid_sync(a, tgt, m.flag, rows_qkv, n_qkv)) return;
         if (attn_block) attention_head<D>(a, l, blockIdx.x, awork, cache_len, total_len);
@@ -610,7 +614,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
         if (!gemv_job(a, 4 * l + 1, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
         if (!grid_sync(a, tgt, m.flag, rows_h, n_h)) return;
         load_vec(m, a.hidden, a.H, true);
-        prologue(m, a.H, ly.post_norm, a.eps, nw_post);
+        prologue(m, a.H, post_norm, a.eps, nw_post);
         if (!gemv_job(a, 4 * l + 2, kEpiGlu, m, ring, full, empty, kslot, a.gated, best)) return;
         if (!grid_sync(a, tgt, m.flag, rows_gu, n_gu)) return;
         load_vec(m, a.gated, a.F, false);
