@@ -14,6 +14,8 @@ Weights (596 MB INT8 + 37 MB scales) exceed the 126 MB L2, so no L2 flush is nee
 
 N > 1 GPUs (torchrun): every rank serves its own independent request stream on its own
 GPU (replicas, no collective on the data path); value = all ranks' tokens / max rank time.
+The line also carries `dp_batched`: config 4 (Llama-3.2-1B INT4, 256 sequences of 1024
+context in total) split data-parallel over the N ranks, aggregate decode tok/s.
 
 `--impl reference` times the CPU restatement of the reference kernels (oracle/, the
 reference's NEON code does not build on x86) on the host cores, rank 0 only.
@@ -47,6 +49,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline sample")
     ap.add_argument("--no-kernel-timing", action="store_true")
+    ap.add_argument("--no-dp-batched", action="store_true",
+                    help="omit the dp_batched object (config 4, 256 sequences split over the ranks)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only time the GEMV kernel class (one token's projections) and print its roofline")
     ap.add_argument("--gemv-lm", action="store_true",
@@ -193,6 +197,27 @@ def gemv_kernel_timing(arch, dev_index, layers=0):
     return {"launches": len(shapes), "bytes": total_bytes, "ms": ms}
 
 
+def host_cpu():
+    """The host the CPU baseline ran on: architecture, CPU model and the SIMD ISA flags that
+    matter for the restatement (it is portable C; the reference's NEON code needs aarch64)."""
+    info = {"arch": os.uname().machine, "model": None, "isa": []}
+    try:
+        with open("/proc/cpuinfo") as f:
+            txt = f.read()
+        for line in txt.splitlines():
+            if line.startswith("model name") and info["model"] is None:
+                info["model"] = line.split(":", 1)[1].strip()
+            if line.startswith(("flags", "Features")):
+                flags = set(line.split(":", 1)[1].split())
+                keep = ("sse4_2", "avx", "avx2", "fma", "f16c", "avx512f", "avx512bw", "avx512_vnni", "avx512_fp16",
+                        "avx512_bf16", "amx_int8", "amx_bf16", "asimd", "asimddp", "i8mm", "fphp", "asimdhp", "sve")
+                info["isa"] = [k for k in keep if k in flags]
+                break
+    except OSError:
+        pass
+    return info
+
+
 def cpu_baseline_sample(folder, prompt, n_tokens=4):
     """Decode tok/s of the CPU restatement (all host threads), bounded sample."""
     from oracle import model as OM
@@ -206,7 +231,8 @@ def cpu_baseline_sample(folder, prompt, n_tokens=4):
     for _ in range(n_tokens):
         tok = m.decode_argmax([tok])
     dt = time.perf_counter() - t0
-    return {"value": n_tokens / dt, "unit": "tok/s", "cores": refcpu.threads(), "kind": "port",
+    return {"value": n_tokens / dt, "unit": "tok/s", "cores": refcpu.threads(), "kind": "port", "host": host_cpu(),
+            "context": f"{len(prompt)}..{len(prompt) + n_tokens - 1}",
             "sample": f"{n_tokens} greedy decode tokens after a {len(prompt) - 1}-token prefill, Qwen3-0.6B INT8 "
                       f"G{GROUP}, oracle/refcpu (C, OpenMP) restatement of the reference kernels; the NEON "
                       "reference does not build on x86"}
@@ -244,7 +270,11 @@ def run_reference(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic (random-init weights, random ids)",
             "impl": "reference",
             "config": {"workload": f"qwen3-0.6b int8 g{GROUP} batch1 prompt{PROMPT} decode", "parallelism": "cpu"},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": refcpu.threads(), "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": refcpu.threads(), "kind": "port", "sample": sample,
+                             "host": host_cpu()},
+            "config_note": (f"same model, weights and greedy decode as the GPU arm; each step decodes {per_step} "
+                            f"tokens at contexts {PROMPT}..{PROMPT + per_step * (args.warmup + args.steps)} "
+                            f"(the GPU arm decodes {DECODE} per request at contexts {PROMPT}..{PROMPT + DECODE - 1})"),
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -535,6 +565,56 @@ def run_config4(args):
     return 0
 
 
+def dp_batched_measure(rank, world, barrier, pg, B=256, P=1024, NEW=32):
+    """The data-parallel split of batched decode (config 4 at B sequences in total): each rank
+    decodes its contiguous shard of ceil(B/N) independent sequences (1024-token random contexts,
+    full cache, NEW greedy steps) with no collective on the data path. One untimed warm-up
+    request, then one timed request; decode time from CUDA events on each rank's engine stream,
+    max over ranks. Returns the dict for rank 0 (None elsewhere)."""
+    import torch
+    from cactus_b200 import convert, dist
+    hbm, _, src = _peaks()
+    arch = convert.llama3_2_1b(GROUP)
+    s0, s1 = dist.shard(B, rank, world)
+    bg = s1 - s0
+    eng = _engine_for(arch, rank, barrier, P + NEW + 8, max(1, -(-B // world)), torch.cuda.current_device())
+    eng.set_cache_window(0, 0)
+    rng = np.random.default_rng(4000 + B)
+    prompts = rng.integers(0, arch.vocab_size, (B, P)).astype(np.uint32)[s0:s1]
+    dec = pre = 0.0
+    for it in range(2):
+        if bg == 1:
+            eng.generate_greedy(prompts[0], NEW)
+        elif bg > 1:
+            eng.generate_batch_greedy(prompts, NEW)
+        if bg and it == 1:
+            st = eng.stats()
+            dec, pre = st["decode_ms"], st["prefill_ms"]
+    eng.close()
+    t = torch.tensor([dec, pre], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    barrier()
+    if rank != 0:
+        return None
+    H, F, D, Hq, Hkv, V = arch.hidden_dim, arch.ffn_intermediate_dim, arch.attention_head_dim, arch.attention_heads, \
+        arch.attention_kv_heads, arch.vocab_size
+    w = arch.num_layers * ((Hq + 2 * Hkv) * D * H + H * Hq * D + 3 * F * H) + V * H
+    step_w_bytes = w // 2 + w // GROUP * 2
+    kv_seq = arch.num_layers * (P + NEW / 2) * Hkv * (2 * D + 2 * 4 * ((D + 127) // 128))
+    dmax, pmax = t[0].item(), t[1].item()
+    step_s = dmax / 1e3 / NEW
+    per_gpu_bytes = step_w_bytes + kv_seq * -(-B // world)
+    return {"workload": f"llama3.2-1b int4 g{GROUP} batched greedy decode, {B} sequences in total, context {P}, "
+                        f"{NEW} steps", "metric": "aggregate decode tok/s", "value": B * NEW / (dmax / 1e3),
+            "unit": "tok/s", "n_gpus": world, "batch_per_gpu": -(-B // world), "ms_per_decode_step": step_s * 1e3,
+            "prefill_tok_s": B * (P - 1) / (pmax / 1e3),
+            "per_gpu_bytes_per_step": per_gpu_bytes, "per_gpu_achieved_gbs": per_gpu_bytes / step_s / 1e9,
+            "per_gpu_frac_of_hbm": per_gpu_bytes / step_s / 1e9 / hbm, "peak_source": src,
+            "parallelism": f"dp{world} (contiguous sequence shards, no collective)", "scaling": "strong",
+            "warmup": 1, "steps": 1}
+
+
 def run_gemv_lm(args):
     """The grouped INT8 GEMV alone on the Qwen3-0.6B lm-head shape (M=1, K=1024, N=151936,
     G=32: 165.3 MB of weights + scales, above the 126 MB L2; two weight copies alternate), one
@@ -723,6 +803,10 @@ def main():
             except Exception as e:  # report, do not hide
                 out["cpu_baseline"] = {"error": str(e)}
     eng.close()
+    if not args.no_dp_batched:
+        dp = dp_batched_measure(rank, world, barrier, pg)
+        if out is not None:
+            out["dp_batched"] = dp
     if pg:
         pg.barrier()
         pg.destroy_process_group()

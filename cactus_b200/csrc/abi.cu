@@ -414,10 +414,6 @@ CB_API int cactus_cuda_sample_f16(const uint16_t* logits, size_t rows, size_t vo
         cb::launch_argmax(H(last), (int)vocab, out_index, S(stream));
         return check_launch("sample_f16");
     }
-    if (top_p > 0.0f && top_p < 1.0f && (top_k == 0 || top_k > 1000))
-        return fail(CB_ERR_UNSUPPORTED, "sample: top_p filtering needs 0 < top_k <= 1000");
-    if (top_k > 1000 || (top_k == 0 && top_p >= 1.0f && vocab > 1000))
-        return fail(CB_ERR_UNSUPPORTED, "sample: more than 1000 candidates are not supported");
     if (!work) return fail(CB_ERR_ARG, "sample: scratch buffer required");
     cb::launch_sample(H(last), (int)vocab, temperature, top_p, (int)top_k, uniform, history, (int)n_history, H(work),
                       out_index, S(stream));
@@ -432,6 +428,32 @@ __device__ __align__(256) uint16_t g_sample_scratch[kStaticSampleVocab];
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};  // id of the context the address belongs to
+
+// Unique id of the calling thread's current context (cuCtxGetId, reached through the
+// runtime's driver entry points so the library does not link libcuda). A device reset
+// creates a new context with a new id, which invalidates a resolved symbol address.
+bool current_context_id(unsigned long long* id) {
+    using get_cur_t = int (*)(void**);
+    using get_id_t = int (*)(void*, unsigned long long*);
+    static get_cur_t get_cur = nullptr;
+    static get_id_t get_id = nullptr;
+    if (!get_cur || !get_id) {
+        void* f1 = nullptr;
+        void* f2 = nullptr;
+        cudaDriverEntryPointQueryResult q1, q2;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) != cudaSuccess ||
+            cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) != cudaSuccess || !f1 || !f2) {
+            cudaGetLastError();
+            return false;
+        }
+        get_cur = reinterpret_cast<get_cur_t>(f1);
+        get_id = reinterpret_cast<get_id_t>(f2);
+    }
+    void* ctx = nullptr;
+    if (get_cur(&ctx) != 0 || !ctx) return false;
+    return get_id(ctx, id) == 0;
+}
 }  // namespace
 
 CB_API int cactus_cuda_sample_f16_noalloc(const uint16_t* logits, size_t rows, size_t vocab, float temperature,
@@ -448,8 +470,13 @@ CB_API int cactus_cuda_sample_f16_noalloc(const uint16_t* logits, size_t rows, s
     }
     void* scratch = nullptr;
     {
-        // set-up on the first call per device: resolve the array's address once
+        // set-up on the first call per device (and again after a device reset replaced the
+        // context): resolve the array's address with the device current
         std::lock_guard<std::mutex> lk(g_scratch_mu);
+        if (g_scratch_ptr[dev]) {
+            unsigned long long ctx = 0;
+            if (!current_context_id(&ctx) || ctx != g_scratch_ctx[dev]) g_scratch_ptr[dev] = nullptr;
+        }
         if (!g_scratch_ptr[dev]) {
             void* p = nullptr;
             const cudaError_t e = cudaGetSymbolAddress(&p, g_sample_scratch);
@@ -458,7 +485,11 @@ CB_API int cactus_cuda_sample_f16_noalloc(const uint16_t* logits, size_t rows, s
                 return fail(CB_ERR_LAUNCH, std::string("sample_noalloc: cudaGetSymbolAddress failed: ") +
                                                cudaGetErrorString(e));
             }
+            unsigned long long ctx = 0;
+            if (!current_context_id(&ctx))
+                return fail(CB_ERR_LAUNCH, "sample_noalloc: cannot identify the current CUDA context");
             g_scratch_ptr[dev] = p;
+            g_scratch_ctx[dev] = ctx;
         }
         scratch = g_scratch_ptr[dev];
     }

@@ -705,7 +705,6 @@ uint32_t Engine::decode(const uint32_t* tokens, size_t n, float temperature, flo
     const bool greedy = temperature == 0.0f && top_p <= 0.0f && top_k == 0;
     if (greedy) return decode_argmax(tokens, n, entropy);
     pdl_scope pdl(use_pdl_);
-    if (top_k > 1000) throw std::runtime_error("top_k above 1000 is not supported by the device sampler");
     if (n == 0) throw std::runtime_error("Token sequence cannot be empty");
     run_forward_tokens(tokens, 1, (int)n);
     gather_last(1, (int)n);

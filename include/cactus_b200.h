@@ -130,8 +130,9 @@ CB_API int cactus_cuda_argmax_f16(const uint16_t* logits, size_t rows, size_t vo
 
 /* ---- non-greedy sampling: cactus_sample_f16 (kernel_nn.cpp:469-651) on row `rows-1`:
  *      temperature (fp16 multiply), repetition penalty 1.1 over `history`, top-k, top-p
- *      (requires 0 < top_k <= 1000 when 0 < top_p < 1), then the first index whose in-order
- *      cumulative probability reaches `uniform` (the reference draws it from std::mt19937).
+ *      (any top_k, including 0 = no top-k, and any number of surviving candidates), then the
+ *      first index whose in-order cumulative probability reaches `uniform` (the reference
+ *      draws it from std::mt19937).
  *      `work` is caller-provided fp16 scratch of `vocab` elements. Greedy arguments
  *      (temperature 0, top_p <= 0, top_k 0) give the first-max argmax. */
 CB_API int cactus_cuda_sample_f16(const uint16_t* logits, size_t rows, size_t vocab, float temperature, float top_p,
@@ -143,7 +144,8 @@ CB_API int cactus_cuda_sample_f16(const uint16_t* logits, size_t rows, size_t vo
  *      inside this library holding up to 262144 fp16 entries per device; larger vocabularies
  *      are rejected with CB_ERR_ARG. Nothing in it needs to start at zero (every entry used is
  *      written before it is read). The first call on each device resolves the array's address
- *      (cudaGetSymbolAddress); make it before any stream capture. Calls that overlap in time
+ *      (cudaGetSymbolAddress); make it before any stream capture. After a device reset the
+ *      next call resolves it again in the new context (so make one call before capturing there too). Calls that overlap in time
  *      on one device (different streams or host threads) share the array and race: serialise
  *      them. Results equal cactus_cuda_sample_f16's. */
 CB_API int cactus_cuda_sample_f16_noalloc(const uint16_t* logits, size_t rows, size_t vocab, float temperature,

@@ -102,6 +102,41 @@ def test_sampler_matches_restatement(temp, top_p, top_k, u):
     assert int(host(out, np.uint32)[0]) == OS.sample_f16(logits, temp, top_p, top_k, u, hist.tolist())
 
 
+@pytest.mark.parametrize("V,temp,top_p,top_k,u,ties", [
+    (5000, 0.7, 0.0, 0, 0.5, 0),        # no top-k, no top-p: all 5000 logits survive
+    (5000, 0.7, 0.0, 0, 0.999, 0),
+    (5000, 1.0, 0.9, 0, 0.3, 0),        # top-p over all logits (no top-k)
+    (5000, 0.0, 0.5, 0, 0.8, 0),        # top-p alone at temperature 0
+    (5000, 0.8, 0.0, 2000, 0.6, 0),     # top-k beyond the shared-memory candidate list
+    (5000, 0.9, 0.7, 1500, 0.4, 0),
+    (5000, 0.7, 0.0, 20, 0.5, 2000),    # 2000 equal logits with top-k 20: ties keep all 2000
+    (5000, 1.0, 0.6, 20, 0.7, 2000),    # the top-p cut falls inside a run of equal values
+    (151936, 0.6, 0.9, 0, 0.42, 0),     # the Qwen vocabulary with top-p only
+])
+def test_sampler_many_candidates_match_restatement(V, temp, top_p, top_k, u, ties):
+    """More survivors than the 1024-entry shared-memory list (kernel_nn.cpp:520-650 with
+    any top_k): the top-p runs and the final in-order draw walk all V entries."""
+    L = cb.lib()
+    rng = np.random.default_rng(V + top_k + ties + int(u * 100))
+    logits = (rng.standard_normal(V) * 3).astype(np.float16)
+    if ties:
+        logits[:] = np.minimum(logits, np.float16(5.0))
+        logits[rng.permutation(V)[:ties]] = np.float16(6.0)
+    hist = rng.integers(0, V, 10).astype(np.uint32)
+    work = empty((V,), np.float16)
+    exp = OS.sample_f16(logits, temp, top_p, top_k, u, hist.tolist())
+    for entry in ("sample", "noalloc"):
+        out = empty((1,), np.uint32)
+        if entry == "sample":
+            cb.check(L.cactus_cuda_sample_f16(ptr(dev(logits)), 1, V, temp, top_p, top_k, u, ptr(dev(hist)),
+                                              len(hist), ptr(work), ptr(out), None))
+        else:
+            cb.check(L.cactus_cuda_sample_f16_noalloc(ptr(dev(logits)), 1, V, temp, top_p, top_k, u,
+                                                      ptr(dev(hist)), len(hist), ptr(out), None))
+        assert int(host(out, np.uint32)[0]) == exp, entry
+    assert L.cactus_cuda_device_error(None) == 0
+
+
 def test_entropy_kernel():
     L = cb.lib()
     rng = np.random.default_rng(4)
