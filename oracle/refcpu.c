@@ -499,36 +499,58 @@ void ref_quantize_kv(const uint16_t* src, int8_t* dst, float* scales, size_t seq
 }
 
 /* ---------------------------------------------------------------- activations / elementwise */
-void ref_silu_f16(const uint16_t* x, uint16_t* y, size_t n) {
-    const size_t vec = (n / 8) * 8;
-    for (size_t i = 0; i < vec; ++i) {
-        float v = h2f(x[i]);
-        float e = ref_fast_exp(-v);
-        float sg = 1.0f / (1.0f + e);
-        y[i] = f2h(v * sg);
+/* cactus_silu_f16 / cactus_gelu_f16 run under parallel_for with SCALAR_EXPENSIVE {2500, 1250}
+ * (kernel_nn.cpp:13,50; kernel_utils.h:410-437, 516-548): from 2500 elements the work is cut
+ * into min(workers, ceil(n / 1250)) equal chunks (the last takes the rest), and every chunk
+ * ends with its own scalar tail of (length % 8) elements on the libm formula. The worker
+ * count is the host's (min(hardware threads, 16)), so those positions follow the host.
+ * g_chunk_pool = 0 (the default) restates one chunk: the vector formula everywhere but the
+ * tensor's own tail, which is also what the GPU computes; g_chunk_pool = P restates the
+ * reference on a host with P pool workers. */
+static int g_chunk_pool = 0;
+void ref_set_chunk_pool(int workers) { g_chunk_pool = workers < 0 ? 0 : workers; }
+
+static int scalar_tail(size_t i, size_t n) {
+    size_t t = 1;
+    if (g_chunk_pool > 0 && n >= 2500) {
+        t = (n + 1249) / 1250;
+        if (t > (size_t)g_chunk_pool) t = (size_t)g_chunk_pool;
     }
-    for (size_t i = vec; i < n; ++i) {
+    const size_t per = n / t;
+    size_t w = i / per;
+    if (w > t - 1) w = t - 1;
+    const size_t start = w * per, end = (w == t - 1) ? n : start + per;
+    return i >= start + ((end - start) / 8) * 8;
+}
+
+void ref_silu_f16(const uint16_t* x, uint16_t* y, size_t n) {
+    for (size_t i = 0; i < n; ++i) {
         float v = h2f(x[i]);
-        float sg = 1.0f / (1.0f + expf_cr(-v));
-        y[i] = f2h(v * sg);
+        if (!scalar_tail(i, n)) {
+            float e = ref_fast_exp(-v);
+            float sg = 1.0f / (1.0f + e);
+            y[i] = f2h(v * sg);
+        } else {
+            float sg = 1.0f / (1.0f + expf_cr(-v));
+            y[i] = f2h(v * sg);
+        }
     }
 }
 
 void ref_gelu_f16(const uint16_t* x, uint16_t* y, size_t n) {
     const float s2p = 0.7978845608028654f, c = 0.044715f;
-    const size_t vec = (n / 8) * 8;
-    for (size_t i = 0; i < vec; ++i) {
+    for (size_t i = 0; i < n; ++i) {
         float v = h2f(x[i]);
-        float v3 = (v * v) * v;
-        float inner = fmaf(c, v3, v);
-        inner = s2p * inner;
-        float t = ref_fast_tanh(inner);
-        y[i] = f2h((0.5f * v) * (1.0f + t));
-    }
-    for (size_t i = vec; i < n; ++i) {
-        float v = h2f(x[i]);
-        float inner = s2p * fmaf((c * v) * v, v, v);
-        y[i] = f2h((0.5f * v) * (1.0f + tanhf_cr(inner)));
+        if (!scalar_tail(i, n)) {
+            float v3 = (v * v) * v;
+            float inner = fmaf(c, v3, v);
+            inner = s2p * inner;
+            float t = ref_fast_tanh(inner);
+            y[i] = f2h((0.5f * v) * (1.0f + t));
+        } else {
+            float inner = s2p * fmaf((c * v) * v, v, v);
+            y[i] = f2h((0.5f * v) * (1.0f + tanhf_cr(inner)));
+        }
     }
 }
 

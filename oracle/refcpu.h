@@ -77,6 +77,7 @@ float ref_fast_exp(float x);
 /* kernel_utils.h:143-163 */
 float ref_fast_tanh(float x);
 /* kernel_nn.cpp:12-44 */
+void ref_set_chunk_pool(int workers);
 void ref_silu_f16(const uint16_t* x, uint16_t* y, size_t n);
 /* kernel_nn.cpp:46-91 */
 void ref_gelu_f16(const uint16_t* x, uint16_t* y, size_t n);

@@ -60,6 +60,7 @@ def _declare(L):
         "ref_fast_exp": (F, [F]),
         "ref_fast_tanh": (F, [F]),
         "ref_silu_f16": (None, [P, P, Z]),
+        "ref_set_chunk_pool": (None, [I]),
         "ref_gelu_f16": (None, [P, P, Z]),
         "ref_add_f16": (None, [P, P, P, Z]),
         "ref_add_f16_clipped": (None, [P, P, P, Z]),
@@ -203,6 +204,12 @@ def _unary(fn, x):
     y = np.empty_like(x)
     fn(_p(x), _p(y), x.size)
     return y
+
+
+def set_chunk_pool(workers: int):
+    """0: SiLU / GELU take the vector formula everywhere but the tensor's own tail (the GPU's
+    rule); P > 0: the reference's worker chunks on a host with P pool workers."""
+    lib().ref_set_chunk_pool(int(workers))
 
 
 def silu(x):
