@@ -17,8 +17,9 @@ GPU (replicas, no collective on the data path); value = all ranks' tokens / max 
 The line also carries `dp_batched`: config 4 (Llama-3.2-1B INT4, 256 sequences of 1024
 context in total) split data-parallel over the N ranks, aggregate decode tok/s.
 
-`--impl reference` times the CPU restatement of the reference kernels (oracle/, the
-reference's NEON code does not build on x86) on the host cores, rank 0 only.
+`--impl reference` times the reference's own C++ compiled here (oracle/_ref, through a portable
+restatement of its NEON intrinsics) on the host cores, rank 0 only; the C restatement of its
+kernels (oracle/refcpu) where that library is absent.
 """
 from __future__ import annotations
 
@@ -239,18 +240,39 @@ def cpu_baseline_sample(folder, prompt, n_tokens=4):
 
 
 def run_reference(args):
+    """The reference arm, rank 0 only. Where oracle/_ref/libcactus_ref.so exists (the
+    reference's own cactus/ C++ compiled from its tree), it times that: Model::prefill and
+    greedy Model::decode steps on all host threads of its thread pool, on the Qwen3-0.6B
+    shape with group-128 weights (the reference's own group size: its NEON matmuls walk a
+    group in 64-element steps, so at group 32 they would read past each group). Otherwise it
+    times the C restatement (oracle/refcpu) on the group-32 model."""
     rank, _, world = dist_env()
     if rank != 0:
         return 0
-    arch, folder = model_folder()
     from cactus_b200 import convert
+    from oracle import ref as RF
+    os.environ.setdefault("CACTUS_B200_MODELS", "/tmp/cactus_b200_models")
+    use_ref = RF.available()
+    group = 128 if use_ref else GROUP
+    arch = convert.qwen3_0_6b(group)
+    folder = convert.default_model_dir(arch, seed=0)
     convert.make_model(folder, arch, seed=0)
-    from oracle import model as OM
-    from oracle import refcpu
-    refcpu.set_threads(os.cpu_count() or 1)
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, arch.vocab_size, PROMPT).tolist()
-    m = OM.RefModel(folder, context_size=512)
+    if use_ref:
+        m = RF.RefEngine(folder, arch.vocab_size, context_size=512)
+        m.reset()
+        cores, kind = RF.pool_workers(), "reference"
+        what = ("the reference's own C++ (cactus/kernel, graph, engine, models) compiled here with g++ -O3 "
+                "-march=x86-64-v3 against oracle/neon_shim (a portable restatement of its NEON intrinsics); its "
+                "thread pool over all host threads")
+    else:
+        from oracle import model as OM
+        from oracle import refcpu
+        refcpu.set_threads(os.cpu_count() or 1)
+        m = OM.RefModel(folder, context_size=512)
+        cores, kind = refcpu.threads(), "port"
+        what = "oracle/refcpu C restatement, OpenMP over all host threads"
     m.prefill(prompt[:-1])
     tok = prompt[-1]
     per_step = 2
@@ -263,20 +285,23 @@ def run_reference(args):
             tok = m.decode_argmax([tok])
     dt = time.perf_counter() - t0
     v = args.steps * per_step / dt
-    sample = (f"{per_step} greedy decode tokens per step after a {PROMPT - 1}-token prefill (Qwen3-0.6B INT8 G{GROUP}); "
-              "oracle/refcpu C restatement, OpenMP over all host threads (NEON reference does not build on x86)")
+    sample = (f"{per_step} greedy decode tokens per step after a {PROMPT - 1}-token prefill (Qwen3-0.6B INT8 "
+              f"G{group}); {what}")
     line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic (random-init weights, random ids)",
             "impl": "reference",
-            "config": {"workload": f"qwen3-0.6b int8 g{GROUP} batch1 prompt{PROMPT} decode", "parallelism": "cpu"},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": refcpu.threads(), "kind": "port", "sample": sample,
+            "config": {"workload": f"qwen3-0.6b int8 g{group} batch1 prompt{PROMPT} decode", "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample,
                              "host": host_cpu()},
-            "config_note": (f"same model, weights and greedy decode as the GPU arm; each step decodes {per_step} "
-                            f"tokens at contexts {PROMPT}..{PROMPT + per_step * (args.warmup + args.steps)} "
-                            f"(the GPU arm decodes {DECODE} per request at contexts {PROMPT}..{PROMPT + DECODE - 1})"),
+            "config_note": (f"same model shape and greedy decode as the GPU arm (group {group} here, {GROUP} there); "
+                            f"each step decodes {per_step} tokens at contexts {PROMPT}.."
+                            f"{PROMPT + per_step * (args.warmup + args.steps)} (the GPU arm decodes {DECODE} per "
+                            f"request at contexts {PROMPT}..{PROMPT + DECODE - 1})"),
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+    if use_ref:
+        m.close()
     return 0
 
 
