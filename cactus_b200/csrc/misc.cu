@@ -340,6 +340,79 @@ __global__ void matmul_f16_kernel(const __half* __restrict__ A, const __half* __
     }
 }
 
+// Few-row variant (M <= 8, K % 8 == 0): one thread per output column n computes all 8 fp16
+// lanes of the reference's accumulators itself, as four half2 FMAs per 8-element chunk (each
+// lane one fp16 fused multiply-add with a single rounding, in the reference's k order), so
+// the weight row streams as 16-byte loads. Lanes fold with the same hsum tree. The A rows
+// sit in shared memory and every thread reads them as broadcasts.
+template <int MR>
+__global__ void __launch_bounds__(256) matmul_f16_rows_kernel(const __half* __restrict__ A,
+                                                              const __half* __restrict__ Bt, __half* __restrict__ C,
+                                                              int M, int K, int N) {
+    pdl_launch_dependents();
+    extern __shared__ __align__(16) uint8_t smem_f16[];
+    __half* sa = reinterpret_cast<__half*>(smem_f16);
+    pdl_wait();
+    {
+        const int4* a4 = reinterpret_cast<const int4*>(A);
+        int4* s4 = reinterpret_cast<int4*>(sa);
+        for (int i = threadIdx.x; i < M * K / 8; i += blockDim.x) s4[i] = __ldg(a4 + i);
+    }
+    __syncthreads();
+    const long long n = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const __half* b = Bt + n * (long long)K;
+    const int K16 = (K / 16) * 16, K8 = (K / 8) * 8;
+    __half2 acc[MR][4];
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[m][i] = __float2half2_rn(0.0f);
+#pragma unroll 4
+    for (int k = 0; k < K16; k += 16) {
+        const int4 blo = __ldg(reinterpret_cast<const int4*>(b + k));
+        const int4 bhi = __ldg(reinterpret_cast<const int4*>(b + k + 8));
+        const __half2* bl = reinterpret_cast<const __half2*>(&blo);
+        const __half2* bh = reinterpret_cast<const __half2*>(&bhi);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            if (m < M) {
+                const int4 alo = *reinterpret_cast<const int4*>(sa + m * K + k);
+                const int4 ahi = *reinterpret_cast<const int4*>(sa + m * K + k + 8);
+                const __half2* al = reinterpret_cast<const __half2*>(&alo);
+                const __half2* ah = reinterpret_cast<const __half2*>(&ahi);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[m][i] = __hfma2(al[i], bl[i], acc[m][i]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[m][i] = __hfma2(ah[i], bh[i], acc[m][i]);
+            }
+        }
+    }
+    if (K8 > K16) {
+        const int4 bv = __ldg(reinterpret_cast<const int4*>(b + K16));
+        const __half2* bp = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            if (m < M) {
+                const int4 av = *reinterpret_cast<const int4*>(sa + m * K + K16);
+                const __half2* ap = reinterpret_cast<const __half2*>(&av);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[m][i] = __hfma2(ap[i], bp[i], acc[m][i]);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+        if (m < M) {
+            // hsum_f16x8 (kernel_gemm.cpp:8-15): lanes (i, i+4), then (0+2, 1+3), then 0+1
+            const __half2 s01 = __hadd2(acc[m][0], acc[m][2]);  // (l0+l4, l1+l5)
+            const __half2 s23 = __hadd2(acc[m][1], acc[m][3]);  // (l2+l6, l3+l7)
+            const __half2 u = __hadd2(s01, s23);
+            C[(size_t)m * N + n] = __hadd(__low2half(u), __high2half(u));
+        }
+    }
+}
+
 }  // namespace cb
 
 // ==================================================================== host launchers
@@ -414,6 +487,16 @@ int launch_unpack_int4(const uint8_t* p, int8_t* o, long long count, cudaStream_
     return 0;
 }
 int launch_matmul_f16(const __half* A, const __half* Bt, __half* C, int M, int K, int N, cudaStream_t st) {
+    // few rows with 16-byte aligned weight rows and no scalar K tail: the row-streaming kernel
+    if (M <= 8 && K % 8 == 0 && (size_t)M * K * 2 <= 48 * 1024) {
+        const dim3 grid(nblocks(N, 256)), block(256);
+        const size_t sm = (size_t)M * K * 2;
+        if (M == 1) launch_k(matmul_f16_rows_kernel<1>, grid, block, sm, st, A, Bt, C, M, K, N);
+        else if (M <= 2) launch_k(matmul_f16_rows_kernel<2>, grid, block, sm, st, A, Bt, C, M, K, N);
+        else if (M <= 4) launch_k(matmul_f16_rows_kernel<4>, grid, block, sm, st, A, Bt, C, M, K, N);
+        else launch_k(matmul_f16_rows_kernel<8>, grid, block, sm, st, A, Bt, C, M, K, N);
+        return 0;
+    }
     launch_k(matmul_f16_kernel, dim3(nblocks((long long)N * 8, 256)), dim3(256), 0, st, A, Bt, C, M, K, N);
     return 0;
 }

@@ -120,7 +120,8 @@ def test_matmul_rejects_bad_shapes(L):
     assert rc != 0 and b"multiple" in L.cactus_cuda_last_error()
 
 
-@pytest.mark.parametrize("M,K,N", [(1, 640, 1000), (3, 64, 37), (2, 100, 9)])
+@pytest.mark.parametrize("M,K,N", [(1, 640, 1000), (3, 64, 37), (2, 100, 9), (1, 640, 262144), (5, 648, 77),
+                                   (8, 136, 33), (4, 640, 1001), (9, 64, 40), (2, 24, 300)])
 def test_matmul_f16_bit_exact(L, ref, M, K, N):
     rng = np.random.default_rng(K)
     A = f16(rng, (M, K))
