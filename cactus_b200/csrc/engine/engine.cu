@@ -386,6 +386,7 @@ void Engine::setup_persistent() {
 bool Engine::is_global(int layer) const { return cfg_.model_type == kGemma && ((layer + 1) % 6) == 0; }
 
 void Engine::reset() {
+    seq0_ = 0;
     cache_len_ = 0;
     total_len_ = 0;
     push_state(0);
@@ -466,10 +467,10 @@ void Engine::forward(int B, int S, bool graph_mode) {
         const LayerW& lw = layers_[l];
         __half* kl = kall_ + (size_t)l * kv_rows_stride;
         __half* vl = vall_ + (size_t)l * kv_rows_stride;
-        int8_t* kcl = kc_ + (size_t)l * max_batch_ * cache_bstride_;
-        int8_t* vcl = vc_ + (size_t)l * max_batch_ * cache_bstride_;
-        float* ksl = ks_ + (size_t)l * max_batch_ * scale_bstride_;
-        float* vsl = vs_ + (size_t)l * max_batch_ * scale_bstride_;
+        int8_t* kcl = kc_ + ((size_t)l * max_batch_ + seq0_) * cache_bstride_;
+        int8_t* vcl = vc_ + ((size_t)l * max_batch_ + seq0_) * cache_bstride_;
+        float* ksl = ks_ + ((size_t)l * max_batch_ + seq0_) * scale_bstride_;
+        float* vsl = vs_ + ((size_t)l * max_batch_ + seq0_) * scale_bstride_;
 
         gemv(lw.qkv, kProRmsNormQuant, kEpiStore, hidden_, lw.in_norm, qkv_, nullptr, rows);
         QkvPostArgs qa = {};
@@ -781,21 +782,24 @@ void Engine::generate(const uint32_t* prompts, int B, size_t P, size_t max_new, 
     const long long launches0 = launches_;
     long long replays = 0;
     ck(cudaEventRecord(ev_[0], stream_), "event");
-    // prefill prompt[:-1] of every sequence (chunks of 256 rows in total)
+    // prefill prompt[:-1] of every sequence as Model::prefill does it for one sequence
+    // (engine_model.cpp:170-219): chunks of 256 tokens, each sequence into its own cache slot,
+    // so every sequence sees the reference's chunking whatever the batch size
     if (P > 1) {
         const size_t pre = P - 1;
-        const size_t chunk = std::max<size_t>(1, (size_t)max_rows_ / B);
-        std::vector<uint32_t> buf;
-        size_t done = 0;
+        const size_t chunk = std::min<size_t>(256, (size_t)max_rows_);
         const size_t full = pre > chunk ? (pre - 1) / chunk : 0;
-        for (size_t c = 0; c <= full; ++c) {
-            const size_t s0 = c * chunk;
-            const size_t sl = (c == full) ? pre - s0 : chunk;
-            buf.resize((size_t)B * sl);
-            for (int b = 0; b < B; ++b) std::memcpy(&buf[(size_t)b * sl], prompts + (size_t)b * P + s0, sl * 4);
-            run_forward_tokens(buf.data(), B, (int)sl);
-            done += sl;
+        for (int b = 0; b < B; ++b) {
+            cache_len_ = 0;
+            total_len_ = 0;
+            seq0_ = b;
+            for (size_t c = 0; c <= full; ++c) {
+                const size_t s0 = c * chunk;
+                const size_t sl = (c == full) ? pre - s0 : chunk;
+                run_forward_tokens(prompts + (size_t)b * P + s0, 1, (int)sl);
+            }
         }
+        seq0_ = 0;
     }
     // last prompt token of each sequence -> tok_in_
     std::vector<uint32_t> last(B);

@@ -119,6 +119,7 @@ private:
     float attention_scale_ = 1.0f;
     size_t window_ = 512, sink_ = 4, cap_ = 512;
     long long cache_bstride_ = 0, scale_bstride_ = 0;
+    int seq0_ = 0;  // cache slot of sequence 0 of the current forward (per-sequence prefill)
     int8_t *kc_ = nullptr, *vc_ = nullptr;
     float *ks_ = nullptr, *vs_ = nullptr;
     uint8_t* tmp_kv_ = nullptr;
