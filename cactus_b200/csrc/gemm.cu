@@ -210,14 +210,13 @@ int launch_one(const GemmArgs& g, cudaStream_t st) {
 }
 }  // namespace
 
-// CACTUS_B200_GEMM=tc routes the INT8 shapes it supports to the tcgen05 kernel (gemm_tc.cu).
-// Off by default: measured on B200 it runs at about half the mma.sync kernel's rate at every
-// M from 128 to 4096 (operand staging through cp.async bounds both; the tcgen05 tile is
-// 128 x 16, so A is re-staged for every 16 output columns).
+// The tcgen05 GEMM (gemm_tc.cu: TMA-fed tcgen05.mma, TMEM group accumulators) takes every
+// INT8 shape it supports; CACTUS_B200_GEMM=mma keeps this file's mma.sync kernel instead
+// (read once per process).
 bool gemm_tc_enabled() {
     static const bool on = [] {
         const char* e = std::getenv("CACTUS_B200_GEMM");
-        return e && std::string(e) == "tc";
+        return !(e && std::string(e) == "mma");
     }();
     return on;
 }
@@ -237,8 +236,10 @@ int launch_gemm_tc(const int8_t* aq, const float* as, const int8_t* w, const __h
 int launch_gemm(const int8_t* aq, const float* as, const void* w, const __half* ws, __half* out, const __half* resid,
                 int M, int K, int N, int G, int int4, int epi, cudaStream_t st) {
     if (gemm_check(M, K, N, G, int4)) return -1;
-    if (gemm_tc_enabled() && gemm_tc_ok(M, K, N, G, int4))
-        return launch_gemm_tc(aq, as, static_cast<const int8_t*>(w), ws, out, resid, M, K, N, G, epi, st);
+    if (gemm_tc_enabled() && gemm_tc_ok(M, K, N, G, int4)) {
+        const int rc = launch_gemm_tc(aq, as, static_cast<const int8_t*>(w), ws, out, resid, M, K, N, G, epi, st);
+        if (rc != -2) return rc;  // -2: operands not addressable by a tensor map; mma.sync below
+    }
     GemmArgs g = {aq, as, w, ws, out, resid, M, K, N, G, gemm_gpc(K, G)};
     switch (epi * 2 + (int4 ? 1 : 0)) {
         case kEpiStore * 2: return launch_one<kEpiStore, 0>(g, st);

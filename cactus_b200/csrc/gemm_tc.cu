@@ -1,41 +1,55 @@
-// Grouped INT8 GEMM for M >= 64 rows on the 5th-generation tensor cores (tcgen05, TMEM).
+// Grouped INT8 / INT4 GEMM for prefill and batched rows on the 5th-generation tensor cores:
+// TMA-fed tcgen05.mma.kind::i8 with TMEM accumulators, warp-specialised.
 //
-// Result bits are those of qgemm_kernel / qgemv_kernel (and of cactus_matmul_int8,
-// kernel_gemm.cpp:128-327): C[m,n] = fp16(chain_g(fma(float(gsum[m,n,g]), Bs[n,g], acc)) * As[m]).
+// Result bits are those of qgemm_kernel / qgemv_kernel and of cactus_matmul_int8 / _int4
+// (kernel_gemm.cpp:128-529): C[m,n] = fp16(chain_g(fma(float(gsum[m,n,g]), Bs[n,g], acc)) * As[m]).
 // The reference needs the exact int32 sum of every quantisation group before it enters the
-// fp32 chain, so each group gets its own TMEM accumulator: a tcgen05.mma.kind::i8 of K = 32
-// writes (G = 32) or accumulates (G = 64, 128) the group's int32 sums for a 128 x BN tile into
-// its own BN TMEM columns; the epilogue warps read the groups back in order (tcgen05.ld) and
-// continue the fp32 chains in registers — one thread per row.
+// fp32 chain, so every group gets its own TMEM accumulator: the MMAs of group g (one K = 32
+// step for G = 32, two for 64, four for 128, accumulating) write a 128 x 128 int32 tile into
+// one of four TMEM buffers, and the epilogue warps read the groups back in order and continue
+// the fp32 chains in registers while the tensor core fills the next buffers.
 //
-// Per CTA: a 128-row x BN-column output tile, 128 threads (4 warps). K advances in chunks of
-// 128 bytes (4 mma k-steps); chunks are staged with cp.async in the canonical K-major,
-// no-swizzle UMMA layout (8-row x 16-byte core matrices) in a 3-stage ring; the TMEM holds two
-// chunks of group accumulators, so the MMAs of chunk c overlap the epilogue fold of chunk c-1.
-// One thread issues the MMAs; completion is signalled with tcgen05.commit to an mbarrier.
-// Every wait is bounded (device error on timeout) and TMEM is freed on every path.
-// This file is compiled as whole-program device code (build.py WHOLE_PROGRAM): as relocatable
-// code the same MMAs read their shared-memory operands displaced and the products are wrong.
-#include "attention_core.cuh"
+// CTA = 128 activation rows x 128 weight rows, 10 warps:
+//   warp 0  producer: 2-D TMA tile loads (cp.async.bulk.tensor, 128-byte swizzle, no
+//           multicast) of the A and B K-chunks (128 bytes of K) into a 4-stage ring, and the
+//           chunk's fp16 group scales into a scale ring;
+//   warp 1  allocates TMEM (512 columns) and one thread issues the MMAs; tcgen05.commit
+//           signals TMEM buffers full and ring stages free;
+//   warps 2-9  epilogue: warp w reads TMEM lanes 32 * (w % 4) (its tile rows) and columns
+//           64 * ((w - 2) / 4) of each group buffer (tcgen05.ld), continues 64 fp32 chains
+//           per thread, then scales by As and writes fp16 (store / residual / GLU).
+// INT4 weights ([N, K/2] nibbles, low = even k): the producer loads the packed chunk with a
+// 1-D bulk copy and the MMA warp's partner lanes (warp 1, lanes 0-31) unpack it into the
+// swizzled int8 layout before the MMAs (sign-extended nibbles; the group sums are exact).
+// Every wait is bounded; a timeout raises the device error and every role leaves in order
+// (TMEM freed by its allocator after all warps meet).
+// This file is compiled as whole-program device code (build.py WHOLE_PROGRAM).
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+
 #include "common.cuh"
 #include "ops.h"
 
 namespace cb {
 
 namespace {
-constexpr int kTM = 128, kTBN = 16, kTThreads = 128;
-constexpr int kKC = 128;                      // K bytes per chunk (4 x K32 mma steps)
-constexpr int kStages = 3;
-constexpr int kStageA = kTM * kKC;            // 16 KB
-constexpr int kStageB = kTBN * kKC;           // 2 KB
-constexpr int kStageS = kTBN * 4 * 2;         // scales of up to 4 groups x BN columns (fp16)
-constexpr int kStage = ((kStageA + kStageB + kStageS) + 1023) / 1024 * 1024;
-constexpr int kTmemCols = 128;                // 2 chunks x up to 4 groups x 16 columns
+constexpr int kBM = 128, kBN = 128, kKC = 128;  // tile rows (A), tile columns (B rows), K bytes per chunk
+constexpr int kStages = 4;
+constexpr int kTileA = kBM * kKC, kTileB = kBN * kKC;  // 16 KB each
+constexpr int kStage = kTileA + kTileB;                 // 32 KB, 1024-byte aligned
+constexpr int kSStages = 8;                             // scale ring (one slot per chunk)
+constexpr int kSSlot = 4 * kBN * 2;                     // up to 4 groups x 128 columns fp16
+constexpr int kTBufs = 4;                               // TMEM group buffers of 128 columns
+constexpr int kTmemCols = kTBufs * kBN;                 // 512
+constexpr int kWarps = 10, kThreads = kWarps * 32;
+constexpr int kEpiWarps = 8;
+constexpr uint32_t kSpin = 1u << 24;
 
 struct TcArgs {
-    const int8_t* aq;
     const float* as;
-    const int8_t* w;
+    const uint8_t* w4;      // INT4: packed weights [N, K/2]; INT8: null (tensor map B)
     const __half* ws;
     __half* out;
     const __half* resid;
@@ -43,215 +57,329 @@ struct TcArgs {
     int M, K, N, G;
 };
 
-__device__ __forceinline__ void cp_async16_z(void* smem, const void* gmem, unsigned src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
-                 : "memory");
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// smem matrix descriptor, K-major with 128-byte swizzle: 8-row x 128-byte atoms, 1024 bytes
+// between 8-row groups (SBO), version 1, layout type 2 (SWIZZLE_128B). Stage bases are
+// 1024-byte aligned; a K step of 32 bytes inside the atom advances the start address.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// canonical K-major no-swizzle layout: 8-row x 16-byte core matrices, K-columns 128 B apart,
-// 8-row groups (kKC / 16) * 128 B apart
-__device__ __forceinline__ int umma_off(int row, int kc) { return (row >> 3) * (kKC / 16) * 128 + kc * 128 + (row & 7) * 16; }
-
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
-    const uint64_t lbo = 128 >> 4, sbo = ((kKC / 16) * 128) >> 4;
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (lbo << 16) | (sbo << 32) | (1ull << 46);  // version 1, no swizzle
-}
-
-// kind::i8, D = S32, A = B = S8, both K-major, N = kTBN, M = kTM
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTBN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
+// kind::i8: D = S32, A = B = S8, both K-major; N = kBN, M = kBM
+constexpr uint32_t kIdesc =
+    (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 
 __device__ __forceinline__ void tc_mma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n"
         :
-        : "r"(dtmem), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+        : "r"(dtmem), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate));
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// The load and its wait form one asm statement: the destination registers are written
-// asynchronously, and a separate wait statement would let the compiler schedule their first
-// use ahead of it (it only orders memory, not these registers).
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
+// 2-D tiled TMA load of box {kKC bytes, 128 rows} at (x = k byte offset, y = row), no multicast
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// one warp: 64 consecutive TMEM columns of its 32 lanes; load and wait in one statement
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, int (&v)[64]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
         "tcgen05.wait::ld.sync.aligned;"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]),
+          "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]),
+          "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]),
+          "=r"(v[48]), "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]),
+          "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
         : "r"(taddr)
         : "memory");
 }
 
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, unsigned parity, volatile int* abort) {
+    for (uint32_t i = 0; i < kSpin; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 255 && *abort) return false;
+    }
+    *abort = 1;
+    return false;
+}
+
 template <int EPI>
-__global__ void __launch_bounds__(kTThreads, 1) qgemm_tc_kernel(TcArgs a) {
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, TcArgs a) {
     pdl_launch_dependents();
-    pdl_wait();
-    // The declared alignment of dynamic shared memory is not honoured when static shared
-    // variables precede it; the stages are aligned to 1024 bytes by hand (1 KB of slack is
-    // launched) so that operand addresses do not depend on the static layout.
+    // Stage bases must be 1024-byte aligned for the swizzle atoms; the declared alignment of
+    // dynamic shared memory is not relied on (1 KB of slack is launched).
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    __shared__ uint64_t mma_done[2];
+    __half* const sscale = reinterpret_cast<__half*>(smem + kStages * kStage);
+    __shared__ uint64_t full[kStages], empty[kStages], sfull[kSStages], sempty[kSStages], tfull[kTBufs],
+        tempty[kTBufs], drain;
     __shared__ uint32_t tmem_base_s;
-    __shared__ int s_ok;
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTBN;
-    const int G = a.G, ng = a.K / G, gpc = kKC / G, nchunks = a.K / kKC;
+    __shared__ int s_abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+    const int G = a.G, nchunks = a.K / kKC, gpc = kKC / G, spg = G / 32, ngroups = a.K / G;
 
-    if (warp == 0) {  // TMEM for two chunks of group accumulators
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
                      "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (tid == 0) {
-        s_ok = 1;
-        mbar_init(&mma_done[0], 1);
-        mbar_init(&mma_done[1], 1);
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < kSStages; ++s) {
+            mbar_init(&sfull[s], 32);
+            mbar_init(&sempty[s], kEpiWarps);
+        }
+        for (int b = 0; b < kTBufs; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], kEpiWarps);
+        }
+        mbar_init(&drain, 1);
         fence_mbar_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
+    volatile int* const abort = &s_abort;
+    pdl_wait();  // A (and the residual) come from the previous kernel
 
-    auto load = [&](int c) {
-        uint8_t* st = smem + (c % kStages) * kStage;
-        uint8_t* sA = st;
-        uint8_t* sB = st + kStageA;
-        __half* sS = reinterpret_cast<__half*>(st + kStageA + kStageB);
-        const int k0 = c * kKC;
-        for (int i = tid; i < kTM * (kKC / 16); i += kTThreads) {
-            const int r = i >> 3, kc = i & 7, m = m0 + r;
-            cp_async16_z(sA + umma_off(r, kc), a.aq + (size_t)min(m, a.M - 1) * a.K + k0 + kc * 16, m < a.M ? 16u : 0u);
-        }
-        {
-            const int r = tid >> 3, kc = tid & 7;  // kTBN * 8 == kTThreads
-            cp_async16(sB + umma_off(r, kc), a.w + (size_t)(n0 + r) * a.K + k0 + kc * 16);
-        }
-        if (tid < kTBN * gpc) {
-            const int r = tid / gpc, g = tid % gpc;
-            sS[r * 4 + g] = a.ws[(size_t)(n0 + r) * ng + c * gpc + g];
-        }
-        cp_async_commit();
-    };
-
-    float acc[kTBN];
-#pragma unroll
-    for (int j = 0; j < kTBN; ++j) acc[j] = 0.0f;
-    const int row_local = warp * 32 + (tid & 31);                 // TMEM lane = tile row
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-
-    // fold chunk c's group accumulators (in group order) into the per-row fp32 chains
-    auto fold = [&](int c) -> bool {
-        bool ok = true;
-        if (tid == 0) *const_cast<volatile int*>(&s_ok) = mbar_wait_bounded(&mma_done[c & 1], (c >> 1) & 1) ? 1 : 0;
-        __syncthreads();
-        if (!s_ok) return false;
-        mbar_wait_bounded(&mma_done[c & 1], (c >> 1) & 1);  // completed: orders this thread after the MMAs
-        tc_fence_after();
-        const __half* sS = reinterpret_cast<const __half*>(smem + (c % kStages) * kStage + kStageA + kStageB);
-        for (int g = 0; g < gpc; ++g) {
-            int v[16];
-            tmem_ld16(lane_addr + (uint32_t)(((c & 1) * 4 + g) * kTBN), v);
-#pragma unroll
-            for (int j = 0; j < kTBN; ++j) acc[j] = fmaf((float)v[j], __half2float(sS[j * 4 + g]), acc[j]);
-        }
-        tc_fence_before();
-        return ok;
-    };
-
-    bool ok = true;
-    load(0);
-    if (nchunks > 1) load(1);
-    for (int c = 0; c < nchunks && ok; ++c) {
-        if (c + 1 < nchunks) cp_async_wait<1>();
-        else cp_async_wait<0>();
-        fence_proxy_async();  // this thread's cp.async data -> visible to the tensor core
-        __syncthreads();
-        tc_fence_after();
-        if (tid == 0) {
-            const uint32_t base = smem_u32(smem + (c % kStages) * kStage);
-            for (int s = 0; s < kKC / 32; ++s) {
-                const int g = (s * 32) / G;
-                const uint32_t dt = tmem + (uint32_t)(((c & 1) * 4 + g) * kTBN);
-                tc_mma(dt, umma_desc(base + 2 * s * 128), umma_desc(base + kStageA + 2 * s * 128),
-                       (s * 32) % G != 0 ? 1u : 0u);
+    if (warp == 0) {
+        // ---------------------------------------------------------------- producer
+        const uint64_t pol_a = l2_policy_evict_last(), pol_b = l2_policy_evict_first();
+        int issued = 0;
+        for (int c = 0; c < nchunks; ++c) {
+            const int s = c % kStages, ss = c % kSStages;
+            if (c >= kStages && !wait_or_abort(&empty[s], ((c / kStages) - 1) & 1, abort)) break;
+            if (c >= kSStages && !wait_or_abort(&sempty[ss], ((c / kSStages) - 1) & 1, abort)) break;
+            if (lane == 0) {
+                uint8_t* st = smem + s * kStage;
+                mbar_arrive_expect_tx(&full[s], (unsigned)kStage);
+                tma_load_2d(st, &mapA, c * kKC, m0, &full[s], pol_a);
+                tma_load_2d(st + kTileA, &mapB, c * kKC, n0, &full[s], pol_b);
             }
-            tc_commit(&mma_done[c & 1]);
+            ++issued;
+            __half* sl = sscale + ss * (kSSlot / 2);
+            for (int r = lane; r < kBN; r += 32) {
+                const __half* src = a.ws + (size_t)(n0 + r) * ngroups + c * gpc;
+                for (int g = 0; g < gpc; ++g) sl[g * kBN + r] = src[g];
+            }
+            mbar_arrive(&sfull[ss]);
         }
-        if (c >= 1) ok = fold(c - 1);
-        if (ok && c + 2 < nchunks) {
-            __syncthreads();  // every thread has read chunk c-1's scales
-            load(c + 2);      // into the stage of chunk c-1, whose MMAs have completed
+        // no copy may land after the block leaves: wait (bounded) for the last ones issued
+        if (*abort && lane == 0)
+            for (int c = issued > kStages ? issued - kStages : 0; c < issued; ++c)
+                mbar_wait_bounded(&full[c % kStages], (c / kStages) & 1);
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            for (int c = 0; c < nchunks; ++c) {
+                const int s = c % kStages;
+                if (!wait_or_abort(&full[s], (c / kStages) & 1, abort)) break;
+                tc_fence_after();
+                const uint32_t base = smem_u32(smem + s * kStage);
+                bool ok = true;
+                for (int ks = 0; ks < kKC / 32 && ok; ++ks) {
+                    const int kg = c * (kKC / 32) + ks, grp = kg / spg, b = grp % kTBufs;
+                    const bool first = (kg % spg) == 0, last = (kg % spg) == spg - 1;
+                    if (first && grp >= kTBufs) {
+                        ok = wait_or_abort(&tempty[b], ((grp / kTBufs) - 1) & 1, abort);
+                        if (!ok) break;
+                        tc_fence_after();
+                    }
+                    tc_mma(tmem + (uint32_t)(b * kBN), desc_sw128(base + ks * 32), desc_sw128(base + kTileA + ks * 32),
+                           first ? 0u : 1u);
+                    if (last) tc_commit(&tfull[b]);
+                }
+                tc_commit(&empty[s]);
+                if (!ok) break;
+            }
+            // every MMA issued has completed before TMEM is released
+            tc_commit(&drain);
+            mbar_wait_bounded(&drain, 0);
+        }
+        __syncwarp();
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int q = warp & 3, h = (warp - 2) >> 2;
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 64);
+        float run[64];
+#pragma unroll
+        for (int j = 0; j < 64; ++j) run[j] = 0.0f;
+        bool ok = true;
+        for (int grp = 0; grp < ngroups && ok; ++grp) {
+            const int b = grp % kTBufs, c = grp / gpc, gi = grp % gpc, ss = c % kSStages;
+            if (gi == 0) ok = wait_or_abort(&sfull[ss], (c / kSStages) & 1, abort);
+            if (ok) ok = wait_or_abort(&tfull[b], (grp / kTBufs) & 1, abort);
+            if (!ok) break;
+            tc_fence_after();
+            int v[64];
+            tmem_ld64(taddr + (uint32_t)(b * kBN), v);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+            const int4* sc4 = reinterpret_cast<const int4*>(sscale + ss * (kSSlot / 2) + gi * kBN + h * 64);
+#pragma unroll
+            for (int j8 = 0; j8 < 8; ++j8) {
+                const int4 sv = sc4[j8];
+                const __half* sh = reinterpret_cast<const __half*>(&sv);
+#pragma unroll
+                for (int t = 0; t < 8; ++t) run[j8 * 8 + t] = fmaf(i2f_small(v[j8 * 8 + t]), h2f(sh[t]), run[j8 * 8 + t]);
+            }
+            if (gi == gpc - 1) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sempty[ss]);
+            }
+        }
+        const int m = m0 + q * 32 + lane;
+        if (ok && !*abort && m < a.M) {
+            const float asm_ = a.as[m];
+            const int nb = n0 + h * 64;
+            if constexpr (EPI == kEpiGluSilu || EPI == kEpiGluGelu) {
+                int4* o4 = reinterpret_cast<int4*>(a.out + (size_t)m * (a.N / 2) + nb / 2);
+#pragma unroll
+                for (int j8 = 0; j8 < 4; ++j8) {
+                    int4 ov;
+                    __half* oh = reinterpret_cast<__half*>(&ov);
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) {
+                        const int j = j8 * 16 + 2 * t;
+                        const __half g0 = f2h(__fmul_rn(run[j], asm_)), u1 = f2h(__fmul_rn(run[j + 1], asm_));
+                        const __half act = (EPI == kEpiGluSilu) ? ref_silu(g0) : ref_gelu(g0);
+                        oh[t] = __hmul(act, u1);
+                    }
+                    o4[j8] = ov;
+                }
+            } else {
+                int4* o4 = reinterpret_cast<int4*>(a.out + (size_t)m * a.N + nb);
+                const int4* r4 = reinterpret_cast<const int4*>(a.resid + (size_t)m * a.N + nb);
+#pragma unroll
+                for (int j8 = 0; j8 < 8; ++j8) {
+                    int4 ov;
+                    __half* oh = reinterpret_cast<__half*>(&ov);
+                    if constexpr (EPI == kEpiResidual) {
+                        const int4 rv = r4[j8];
+                        const __half* rh = reinterpret_cast<const __half*>(&rv);
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) oh[t] = __hadd(rh[t], f2h(__fmul_rn(run[j8 * 8 + t], asm_)));
+                    } else {
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) oh[t] = f2h(__fmul_rn(run[j8 * 8 + t], asm_));
+                    }
+                    o4[j8] = ov;
+                }
+            }
         }
     }
-    if (ok) ok = fold(nchunks - 1);
-    cp_async_wait<0>();
-    if (!ok && tid == 0) atomicCAS(a.err, 0u, (unsigned)kDevTmaTimeout);
     tc_fence_before();
     __syncthreads();
-    if (warp == 0)
+    if (threadIdx.x == 0 && *abort) atomicCAS(a.err, 0u, (unsigned)kDevTmaTimeout);
+    if (warp == 1) {
+        tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
-    if (!ok) return;
-
-    const int m = m0 + row_local;
-    if (m >= a.M) return;
-    const float asm_ = a.as[m];
-#pragma unroll
-    for (int j = 0; j < kTBN; j += 2) {
-        const int n = n0 + j;
-        const __half v0 = f2h(__fmul_rn(acc[j], asm_)), v1 = f2h(__fmul_rn(acc[j + 1], asm_));
-        if constexpr (EPI == kEpiStore) {
-            a.out[(size_t)m * a.N + n] = v0;
-            a.out[(size_t)m * a.N + n + 1] = v1;
-        } else if constexpr (EPI == kEpiResidual) {
-            a.out[(size_t)m * a.N + n] = __hadd(a.resid[(size_t)m * a.N + n], v0);
-            a.out[(size_t)m * a.N + n + 1] = __hadd(a.resid[(size_t)m * a.N + n + 1], v1);
-        } else {
-            const __half act = (EPI == kEpiGluSilu) ? ref_silu(v0) : ref_gelu(v0);
-            a.out[(size_t)m * (a.N / 2) + n / 2] = __hmul(act, v1);
-        }
     }
 }
 
+// ---------------------------------------------------------------- host side
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry points (the library does not link libcuda)
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return static_cast<EncodeTiled>(nullptr);
+        }
+        return reinterpret_cast<EncodeTiled>(p);
+    }();
+    return fn;
+}
+
+// [rows, kbytes] int8 row-major, box {128 bytes, 128 rows}, 128-byte swizzle; rows past the
+// end read as zeros. The base must be 16-byte aligned and kbytes a multiple of 16.
+bool make_map(CUtensorMap* m, const void* base, int rows, int kbytes) {
+    const EncodeTiled fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15u) || (kbytes % 16)) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)kbytes, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kbytes};
+    const cuuint32_t box[2] = {(cuuint32_t)kKC, 128u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr size_t kSmemBytes = (size_t)kStages * kStage + (size_t)kSStages * kSSlot + 1024;
+
 template <int EPI>
-int launch_tc(const TcArgs& t, cudaStream_t st) {
-    const size_t sm = (size_t)kStages * kStage + 1024;
+int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& t, cudaStream_t st) {
     static bool attr = false;
     if (!attr) {
-        if (cudaFuncSetAttribute(qgemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) !=
+        if (cudaFuncSetAttribute(qgemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
             cudaSuccess)
             return -1;
         attr = true;
     }
-    const dim3 grid((unsigned)(t.N / kTBN), (unsigned)((t.M + kTM - 1) / kTM));
-    launch_k(qgemm_tc_kernel<EPI>, grid, dim3(kTThreads), sm, st, t);
-    return 0;
+    const dim3 grid((unsigned)(t.N / kBN), (unsigned)((t.M + kBM - 1) / kBM));
+    return launch_k(qgemm_tc_kernel<EPI>, grid, dim3(kThreads), kSmemBytes, st, ma, mb, t) == cudaSuccess ? 0 : -1;
 }
 }  // namespace
 
 bool gemm_tc_ok(int M, int K, int N, int G, int int4) {
-    return !int4 && M >= 64 && N % kTBN == 0 && K % kKC == 0 && (G == 32 || G == 64 || G == 128) && K % G == 0;
+    return !int4 && M >= 1 && N % kBN == 0 && K % kKC == 0 && (G == 32 || G == 64 || G == 128) && K % G == 0 &&
+           encode_fn() != nullptr;
 }
 
 int launch_gemm_tc(const int8_t* aq, const float* as, const int8_t* w, const __half* ws, __half* out,
                    const __half* resid, int M, int K, int N, int G, int epi, cudaStream_t st) {
     unsigned* err = dev_error_ptr();
     if (!err) return -1;
-    TcArgs t = {aq, as, w, ws, out, resid, err, M, K, N, G};
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, aq, M, K) || !make_map(&mb, w, N, K)) return -2;  // not TMA-able: caller falls back
+    TcArgs t = {as, nullptr, ws, out, resid, err, M, K, N, G};
     switch (epi) {
-        case kEpiStore: return launch_tc<kEpiStore>(t, st);
-        case kEpiResidual: return launch_tc<kEpiResidual>(t, st);
-        case kEpiGluSilu: return launch_tc<kEpiGluSilu>(t, st);
-        case kEpiGluGelu: return launch_tc<kEpiGluGelu>(t, st);
+        case kEpiStore: return launch_tc<kEpiStore>(ma, mb, t, st);
+        case kEpiResidual: return launch_tc<kEpiResidual>(ma, mb, t, st);
+        case kEpiGluSilu: return launch_tc<kEpiGluSilu>(ma, mb, t, st);
+        case kEpiGluGelu: return launch_tc<kEpiGluGelu>(ma, mb, t, st);
     }
     return -1;
 }

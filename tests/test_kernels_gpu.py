@@ -60,8 +60,8 @@ def _weights(rng, N, K, G, int4=False):
 @pytest.mark.parametrize("M,K,N,G", [(1, 1024, 3072, 32), (1, 1024, 3072, 128), (2, 2048, 1000, 64),
                                       (5, 640, 520, 32), (8, 1024, 4096, 128), (13, 3072, 1024, 32),
                                       (1, 8192, 264, 32),
-                                      # 16 <= M: the mma.sync GEMM (INT4, M < 64, K % 128 != 0) or the
-                                      # tcgen05 GEMM (INT8, M >= 64, K % 128 == 0, G in 32/64/128)
+                                      # 16 <= M: the tcgen05 GEMM (INT8, K % 128 == 0, N % 128 == 0,
+                                      # G in 32/64/128) or the mma.sync GEMM (the rest)
                                       (16, 1024, 3072, 32), (127, 2048, 1024, 32), (64, 3072, 1024, 128),
                                       (33, 640, 512, 32), (200, 1024, 4096, 64), (17, 576, 960, 32),
                                       (130, 1024, 96, 128), (64, 128, 32, 32), (128, 256, 64, 64),
@@ -174,12 +174,13 @@ def test_attention_f16_parity(L, ref, B, S, Skv, Hq, Hkv, D, off, win):
     assert same_bits(got, exp)
 
 
-def test_matmul_tcgen05_path_bit_exact():
-    """The tcgen05 GEMM (opt-in: CACTUS_B200_GEMM=tc, read once per process) on the INT8 GEMM
-    parity cases above, run in a child pytest process."""
-    env = dict(os.environ, CACTUS_B200_GEMM="tc")
+def test_matmul_mma_sync_path_bit_exact():
+    """The mma.sync GEMM (the default for the shapes the tcgen05 GEMM does not take; forced for
+    all with CACTUS_B200_GEMM=mma, read once per process) on the GEMM parity cases above, run
+    in a child pytest process."""
+    env = dict(os.environ, CACTUS_B200_GEMM="mma")
     r = subprocess.run([sys.executable, "-m", "pytest", os.path.abspath(__file__), "-q", "-m", "gpu", "-p",
-                        "no:cacheprovider", "-k", "matmul_prequantized and False"],
+                        "no:cacheprovider", "-k", "matmul_prequantized or config1"],
                        env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
