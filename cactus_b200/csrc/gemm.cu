@@ -230,14 +230,14 @@ const char* gemm_check(int M, int K, int N, int G, int int4) {
 }
 
 bool gemm_tc_ok(int M, int K, int N, int G, int int4);
-int launch_gemm_tc(const int8_t* aq, const float* as, const int8_t* w, const __half* ws, __half* out,
-                   const __half* resid, int M, int K, int N, int G, int epi, cudaStream_t st);
+int launch_gemm_tc(const int8_t* aq, const float* as, const void* w, const __half* ws, __half* out,
+                   const __half* resid, int M, int K, int N, int G, int int4, int epi, cudaStream_t st);
 
 int launch_gemm(const int8_t* aq, const float* as, const void* w, const __half* ws, __half* out, const __half* resid,
                 int M, int K, int N, int G, int int4, int epi, cudaStream_t st) {
     if (gemm_check(M, K, N, G, int4)) return -1;
     if (gemm_tc_enabled() && gemm_tc_ok(M, K, N, G, int4)) {
-        const int rc = launch_gemm_tc(aq, as, static_cast<const int8_t*>(w), ws, out, resid, M, K, N, G, epi, st);
+        const int rc = launch_gemm_tc(aq, as, w, ws, out, resid, M, K, N, G, int4, epi, st);
         if (rc != -2) return rc;  // -2: operands not addressable by a tensor map; mma.sync below
     }
     GemmArgs g = {aq, as, w, ws, out, resid, M, K, N, G, gemm_gpc(K, G)};

@@ -38,9 +38,12 @@ namespace {
 constexpr int kBM = 128, kBN = 128, kKC = 128;  // tile rows (A), tile columns (B rows), K bytes per chunk
 constexpr int kStages = 4;
 constexpr int kTileA = kBM * kKC, kTileB = kBN * kKC;  // 16 KB each
-constexpr int kStage = kTileA + kTileB;                 // 32 KB, 1024-byte aligned
+constexpr int kPackB = kBN * kKC / 2;                  // INT4: the packed chunk, 8 KB
+// a stage: A tile | B tile (int8, swizzled) | INT4 only: the packed B chunk
+template <int I4>
+constexpr int stage_bytes() { return I4 ? kTileA + kTileB + 8192 : kTileA + kTileB; }  // 40 / 32 KB
 constexpr int kSStages = 8;                             // scale ring (one slot per chunk)
-constexpr int kSSlot = 4 * kBN * 2;                     // up to 4 groups x 128 columns fp16
+constexpr int kSSlot = 4 * kBN * 4;                     // up to 4 groups x 128 columns, fp32
 constexpr int kTBufs = 4;                               // TMEM group buffers of 128 columns
 constexpr int kTmemCols = kTBufs * kBN;                 // 512
 constexpr int kWarps = 10, kThreads = kWarps * 32;
@@ -101,24 +104,51 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     return p;
 }
 
-// one warp: 64 consecutive TMEM columns of its 32 lanes; load and wait in one statement
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, int (&v)[64]) {
+// 64 TMEM columns of the warp's 32 lanes set to the integer kBias (a store and its wait)
+__device__ __forceinline__ void tmem_st64_bias(uint32_t taddr) {
+    const int b = 0x4B400000;
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
-        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
+        "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(b)
+        : "memory");
+}
+
+// Two lanes of the fp32 group chain: run = fma(float(gsum), scale, run) for a pair of columns,
+// with one f32x2 subtract and one f32x2 fused multiply-add (each lane rounded as the scalar
+// instruction). The TMEM accumulators start at the integer 0x4B400000, so an accumulated
+// group sum x (|x| < 2^22) reads back as the float 12582912 + x exactly and one subtraction
+// of 12582912 gives float(x) exactly.
+__device__ __forceinline__ void chain2(unsigned long long& run, int v0, int v1, unsigned long long s2,
+                                       unsigned long long bias2) {
+    asm("{\n\t.reg .b64 f;\n\t"
+        "mov.b64 f, {%1, %2};\n\t"
+        "sub.rn.f32x2 f, f, %4;\n\t"
+        "fma.rn.f32x2 %0, f, %3, %0;\n\t}"
+        : "+l"(run)
+        : "r"(v0), "r"(v1), "l"(s2), "l"(bias2));
+}
+
+// one warp: 16 consecutive TMEM columns of its 32 lanes, issued without waiting; the values
+// are valid after tmem_wait_ld on the same array, whose register operands keep every use of
+// them behind the wait
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, int (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]),
-          "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]),
-          "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]),
-          "=r"(v[48]), "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]),
-          "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr)
         : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld(int (&v)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                   "+r"(v[15])
+                 :
+                 : "memory");
 }
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, unsigned parity, volatile int* abort) {
@@ -130,17 +160,39 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, unsigned parity, vo
     return false;
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+// INT4: nibbles of the packed chunk (row-major [128][64] bytes, low nibble = even k) become
+// sign-extended int8 in the swizzled K-major B tile. One 16-byte output chunk (16 k) comes
+// from 8 packed bytes; lane l converts chunks l, l + 32, ... of the 1024.
+__device__ __forceinline__ void unpack_chunk_int4(const uint8_t* packed, uint8_t* btile, int lane) {
+#pragma unroll 4
+    for (int i = 0; i < 32; ++i) {
+        const int idx = lane + 32 * i, r = idx >> 3, j = idx & 7;
+        const uint2 p = *reinterpret_cast<const uint2*>(packed + r * 64 + j * 8);
+        uint4 o;
+        const unsigned lo0 = __vsub4((p.x & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+        const unsigned hi0 = __vsub4(((p.x >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+        const unsigned lo1 = __vsub4((p.y & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+        const unsigned hi1 = __vsub4(((p.y >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+        o.x = __byte_perm(lo0, hi0, 0x5140);
+        o.y = __byte_perm(lo0, hi0, 0x7362);
+        o.z = __byte_perm(lo1, hi1, 0x5140);
+        o.w = __byte_perm(lo1, hi1, 0x7362);
+        *reinterpret_cast<uint4*>(btile + r * 128 + ((j ^ (r & 7)) << 4)) = o;
+    }
+}
+
+template <int EPI, int I4>
+__global__ void __maxnreg__(200)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, TcArgs a) {
     pdl_launch_dependents();
     // Stage bases must be 1024-byte aligned for the swizzle atoms; the declared alignment of
     // dynamic shared memory is not relied on (1 KB of slack is launched).
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    __half* const sscale = reinterpret_cast<__half*>(smem + kStages * kStage);
-    __shared__ uint64_t full[kStages], empty[kStages], sfull[kSStages], sempty[kSStages], tfull[kTBufs],
-        tempty[kTBufs], drain;
+    constexpr int kStage = stage_bytes<I4>();
+    float* const sscale = reinterpret_cast<float*>(smem + kStages * kStage);
+    __shared__ uint64_t full[kStages], empty[kStages], cfull[kStages], sfull[kSStages], sempty[kSStages],
+        tfull[kTBufs], tempty[kTBufs], drain;
     __shared__ uint32_t tmem_base_s;
     __shared__ int s_abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -158,6 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&cfull[s], 1);
         }
         for (int s = 0; s < kSStages; ++s) {
             mbar_init(&sfull[s], 32);
@@ -181,24 +234,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------------------------------------------------------- producer
         const uint64_t pol_a = l2_policy_evict_last(), pol_b = l2_policy_evict_first();
         int issued = 0;
+        // INT4: the chunk loaded one iteration earlier is unpacked after the next one is issued
+        auto convert = [&](int c) -> bool {
+            const int s = c % kStages;
+            if (!wait_or_abort(&full[s], (c / kStages) & 1, abort)) return false;
+            uint8_t* st = smem + s * kStage;
+            unpack_chunk_int4(st + kTileA + kTileB, st + kTileA, lane);
+            fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&cfull[s]);
+            return true;
+        };
         for (int c = 0; c < nchunks; ++c) {
             const int s = c % kStages, ss = c % kSStages;
             if (c >= kStages && !wait_or_abort(&empty[s], ((c / kStages) - 1) & 1, abort)) break;
             if (c >= kSStages && !wait_or_abort(&sempty[ss], ((c / kSStages) - 1) & 1, abort)) break;
             if (lane == 0) {
                 uint8_t* st = smem + s * kStage;
-                mbar_arrive_expect_tx(&full[s], (unsigned)kStage);
-                tma_load_2d(st, &mapA, c * kKC, m0, &full[s], pol_a);
-                tma_load_2d(st + kTileA, &mapB, c * kKC, n0, &full[s], pol_b);
+                if (I4) {
+                    mbar_arrive_expect_tx(&full[s], (unsigned)(kTileA + kPackB));
+                    tma_load_2d(st, &mapA, c * kKC, m0, &full[s], pol_a);
+                    tma_load_2d(st + kTileA + kTileB, &mapB, c * (kKC / 2), n0, &full[s], pol_b);
+                } else {
+                    mbar_arrive_expect_tx(&full[s], (unsigned)kStage);
+                    tma_load_2d(st, &mapA, c * kKC, m0, &full[s], pol_a);
+                    tma_load_2d(st + kTileA, &mapB, c * kKC, n0, &full[s], pol_b);
+                }
             }
             ++issued;
-            __half* sl = sscale + ss * (kSSlot / 2);
+            float* sl = sscale + ss * (kSSlot / 4);
             for (int r = lane; r < kBN; r += 32) {
                 const __half* src = a.ws + (size_t)(n0 + r) * ngroups + c * gpc;
-                for (int g = 0; g < gpc; ++g) sl[g * kBN + r] = src[g];
+                for (int g = 0; g < gpc; ++g) sl[g * kBN + r] = h2f(src[g]);
             }
             mbar_arrive(&sfull[ss]);
+            if (I4 && c >= 1 && !convert(c - 1)) break;
         }
+        if (I4 && !*abort && issued == nchunks) convert(nchunks - 1);
         // no copy may land after the block leaves: wait (bounded) for the last ones issued
         if (*abort && lane == 0)
             for (int c = issued > kStages ? issued - kStages : 0; c < issued; ++c)
@@ -208,20 +280,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             for (int c = 0; c < nchunks; ++c) {
                 const int s = c % kStages;
-                if (!wait_or_abort(&full[s], (c / kStages) & 1, abort)) break;
+                if (!wait_or_abort(I4 ? &cfull[s] : &full[s], (c / kStages) & 1, abort)) break;
                 tc_fence_after();
                 const uint32_t base = smem_u32(smem + s * kStage);
                 bool ok = true;
                 for (int ks = 0; ks < kKC / 32 && ok; ++ks) {
                     const int kg = c * (kKC / 32) + ks, grp = kg / spg, b = grp % kTBufs;
                     const bool first = (kg % spg) == 0, last = (kg % spg) == spg - 1;
-                    if (first && grp >= kTBufs) {
-                        ok = wait_or_abort(&tempty[b], ((grp / kTBufs) - 1) & 1, abort);
+                    if (first) {  // the epilogue has re-armed this buffer with the bias
+                        ok = wait_or_abort(&tempty[b], (grp / kTBufs) & 1, abort);
                         if (!ok) break;
                         tc_fence_after();
                     }
                     tc_mma(tmem + (uint32_t)(b * kBN), desc_sw128(base + ks * 32), desc_sw128(base + kTileA + ks * 32),
-                           first ? 0u : 1u);
+                           1u);
                     if (last) tc_commit(&tfull[b]);
                 }
                 tc_commit(&empty[s]);
@@ -236,35 +308,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------------------------------------------------------- epilogue
         const int q = warp & 3, h = (warp - 2) >> 2;
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 64);
-        float run[64];
-#pragma unroll
-        for (int j = 0; j < 64; ++j) run[j] = 0.0f;
-        bool ok = true;
-        for (int grp = 0; grp < ngroups && ok; ++grp) {
-            const int b = grp % kTBufs, c = grp / gpc, gi = grp % gpc, ss = c % kSStages;
-            if (gi == 0) ok = wait_or_abort(&sfull[ss], (c / kSStages) & 1, abort);
-            if (ok) ok = wait_or_abort(&tfull[b], (grp / kTBufs) & 1, abort);
-            if (!ok) break;
-            tc_fence_after();
-            int v[64];
-            tmem_ld64(taddr + (uint32_t)(b * kBN), v);
+        // arm every group buffer with the bias (completion 0 of tempty)
+        for (int b = 0; b < kTBufs; ++b) {
+            tmem_st64_bias(taddr + (uint32_t)(b * kBN));
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[b]);
-            const int4* sc4 = reinterpret_cast<const int4*>(sscale + ss * (kSSlot / 2) + gi * kBN + h * 64);
+        }
+        const float bias = 12582912.0f;
+        const unsigned long long bias2 =
+            ((unsigned long long)__float_as_uint(bias) << 32) | (unsigned long long)__float_as_uint(bias);
+        unsigned long long run[32];
 #pragma unroll
-            for (int j8 = 0; j8 < 8; ++j8) {
-                const int4 sv = sc4[j8];
-                const __half* sh = reinterpret_cast<const __half*>(&sv);
+        for (int j = 0; j < 32; ++j) run[j] = 0ull;  // two fp32 zeros
+        // Software-pipelined over the groups in slices of 16 columns: the TMEM read of the next
+        // slice is in flight while the current one runs through the chains.
+        auto chains = [&](const int (&v)[16], int grp, int sl) {
+            const int c = grp / gpc, gi = grp % gpc, ss = c % kSStages;
+            const ulonglong2* sc =
+                reinterpret_cast<const ulonglong2*>(sscale + ss * (kSSlot / 4) + gi * kBN + h * 64 + sl * 16);
 #pragma unroll
-                for (int t = 0; t < 8; ++t) run[j8 * 8 + t] = fmaf(i2f_small(v[j8 * 8 + t]), h2f(sh[t]), run[j8 * 8 + t]);
+            for (int j4 = 0; j4 < 4; ++j4) {
+                const ulonglong2 sv = sc[j4];
+                chain2(run[sl * 8 + 2 * j4], v[4 * j4], v[4 * j4 + 1], sv.x, bias2);
+                chain2(run[sl * 8 + 2 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3], sv.y, bias2);
             }
-            if (gi == gpc - 1) {
+        };
+        // slice t = 4 * group + sl; before issuing the first slice of a group, wait until the
+        // group's buffer is full (and, for the first group of a chunk, its scales staged)
+        auto issue = [&](int t, int (&v)[16]) -> bool {
+            const int grp = t >> 2, sl = t & 3, b = grp % kTBufs;
+            if (sl == 0) {
+                const int c = grp / gpc;
+                if (grp % gpc == 0 && !wait_or_abort(&sfull[c % kSStages], (c / kSStages) & 1, abort)) return false;
+                if (!wait_or_abort(&tfull[b], (grp / kTBufs) & 1, abort)) return false;
+                tc_fence_after();
+            }
+            tmem_ld16_issue(taddr + (uint32_t)(b * kBN + sl * 16), v);
+            return true;
+        };
+        // after the last slice of a group: re-arm its buffer, hand it back, free the scale slot
+        auto retire = [&](int grp) {
+            const int b = grp % kTBufs;
+            if (grp + kTBufs < ngroups) tmem_st64_bias(taddr + (uint32_t)(b * kBN));
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+            if (grp % gpc == gpc - 1) {
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sempty[ss]);
+                if (lane == 0) mbar_arrive(&sempty[(grp / gpc) % kSStages]);
             }
+        };
+        const int T = ngroups * 4;
+        int x[16], y[16];
+        bool ok = issue(0, x);
+        for (int grp = 0; grp < ngroups && ok; ++grp) {
+            const int t = grp * 4;
+            tmem_wait_ld(x);
+            ok = issue(t + 1, y);
+            chains(x, grp, 0);
+            if (!ok) break;
+            tmem_wait_ld(y);
+            ok = issue(t + 2, x);
+            chains(y, grp, 1);
+            if (!ok) break;
+            tmem_wait_ld(x);
+            ok = issue(t + 3, y);
+            chains(x, grp, 2);
+            if (!ok) break;
+            tmem_wait_ld(y);
+            retire(grp);
+            if (t + 4 < T) ok = issue(t + 4, x);
+            chains(y, grp, 3);
         }
         const int m = m0 + q * 32 + lane;
+        // column j of this thread's 64: lane (j & 1) of the pair run[j >> 1]
+        auto col = [&](int j) -> float {
+            return __uint_as_float((j & 1) ? (unsigned)(run[j >> 1] >> 32) : (unsigned)(run[j >> 1] & 0xFFFFFFFFull));
+        };
         if (ok && !*abort && m < a.M) {
             const float asm_ = a.as[m];
             const int nb = n0 + h * 64;
@@ -277,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int t = 0; t < 8; ++t) {
                         const int j = j8 * 16 + 2 * t;
-                        const __half g0 = f2h(__fmul_rn(run[j], asm_)), u1 = f2h(__fmul_rn(run[j + 1], asm_));
+                        const __half g0 = f2h(__fmul_rn(col(j), asm_)), u1 = f2h(__fmul_rn(col(j + 1), asm_));
                         const __half act = (EPI == kEpiGluSilu) ? ref_silu(g0) : ref_gelu(g0);
                         oh[t] = __hmul(act, u1);
                     }
@@ -294,10 +415,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int4 rv = r4[j8];
                         const __half* rh = reinterpret_cast<const __half*>(&rv);
 #pragma unroll
-                        for (int t = 0; t < 8; ++t) oh[t] = __hadd(rh[t], f2h(__fmul_rn(run[j8 * 8 + t], asm_)));
+                        for (int t = 0; t < 8; ++t) oh[t] = __hadd(rh[t], f2h(__fmul_rn(col(j8 * 8 + t), asm_)));
                     } else {
 #pragma unroll
-                        for (int t = 0; t < 8; ++t) oh[t] = f2h(__fmul_rn(run[j8 * 8 + t], asm_));
+                        for (int t = 0; t < 8; ++t) oh[t] = f2h(__fmul_rn(col(j8 * 8 + t), asm_));
                     }
                     o4[j8] = ov;
                 }
@@ -333,55 +454,65 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-// [rows, kbytes] int8 row-major, box {128 bytes, 128 rows}, 128-byte swizzle; rows past the
-// end read as zeros. The base must be 16-byte aligned and kbytes a multiple of 16.
-bool make_map(CUtensorMap* m, const void* base, int rows, int kbytes) {
+// [rows, kbytes] bytes row-major, box {box_inner bytes, 128 rows}; rows past the end read as
+// zeros. The base must be 16-byte aligned and kbytes a multiple of 16.
+bool make_map(CUtensorMap* m, const void* base, int rows, int kbytes, int box_inner, bool swizzle) {
     const EncodeTiled fn = encode_fn();
     if (!fn || (reinterpret_cast<uintptr_t>(base) & 15u) || (kbytes % 16)) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)kbytes, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)kbytes};
-    const cuuint32_t box[2] = {(cuuint32_t)kKC, 128u};
+    const cuuint32_t box[2] = {(cuuint32_t)box_inner, 128u};
     const cuuint32_t estr[2] = {1u, 1u};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr size_t kSmemBytes = (size_t)kStages * kStage + (size_t)kSStages * kSSlot + 1024;
+template <int I4>
+constexpr size_t smem_bytes() { return (size_t)kStages * stage_bytes<I4>() + (size_t)kSStages * kSSlot + 1024; }
 
-template <int EPI>
+template <int EPI, int I4>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& t, cudaStream_t st) {
     static bool attr = false;
     if (!attr) {
-        if (cudaFuncSetAttribute(qgemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(qgemm_tc_kernel<EPI, I4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem_bytes<I4>()) != cudaSuccess)
             return -1;
         attr = true;
     }
     const dim3 grid((unsigned)(t.N / kBN), (unsigned)((t.M + kBM - 1) / kBM));
-    return launch_k(qgemm_tc_kernel<EPI>, grid, dim3(kThreads), kSmemBytes, st, ma, mb, t) == cudaSuccess ? 0 : -1;
+    return launch_k(qgemm_tc_kernel<EPI, I4>, grid, dim3(kThreads), smem_bytes<I4>(), st, ma, mb, t) == cudaSuccess
+               ? 0
+               : -1;
+}
+
+template <int I4>
+int launch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& t, int epi, cudaStream_t st) {
+    switch (epi) {
+        case kEpiStore: return launch_tc<kEpiStore, I4>(ma, mb, t, st);
+        case kEpiResidual: return launch_tc<kEpiResidual, I4>(ma, mb, t, st);
+        case kEpiGluSilu: return launch_tc<kEpiGluSilu, I4>(ma, mb, t, st);
+        case kEpiGluGelu: return launch_tc<kEpiGluGelu, I4>(ma, mb, t, st);
+    }
+    return -1;
 }
 }  // namespace
 
 bool gemm_tc_ok(int M, int K, int N, int G, int int4) {
-    return !int4 && M >= 1 && N % kBN == 0 && K % kKC == 0 && (G == 32 || G == 64 || G == 128) && K % G == 0 &&
+    (void)int4;
+    return M >= 1 && N % kBN == 0 && K % kKC == 0 && (G == 32 || G == 64 || G == 128) && K % G == 0 &&
            encode_fn() != nullptr;
 }
 
-int launch_gemm_tc(const int8_t* aq, const float* as, const int8_t* w, const __half* ws, __half* out,
-                   const __half* resid, int M, int K, int N, int G, int epi, cudaStream_t st) {
+int launch_gemm_tc(const int8_t* aq, const float* as, const void* w, const __half* ws, __half* out,
+                   const __half* resid, int M, int K, int N, int G, int int4, int epi, cudaStream_t st) {
     unsigned* err = dev_error_ptr();
     if (!err) return -1;
     CUtensorMap ma, mb;
-    if (!make_map(&ma, aq, M, K) || !make_map(&mb, w, N, K)) return -2;  // not TMA-able: caller falls back
+    if (!make_map(&ma, aq, M, K, kKC, true)) return -2;  // not TMA-able: the caller falls back
+    if (!(int4 ? make_map(&mb, w, N, K / 2, kKC / 2, false) : make_map(&mb, w, N, K, kKC, true))) return -2;
     TcArgs t = {as, nullptr, ws, out, resid, err, M, K, N, G};
-    switch (epi) {
-        case kEpiStore: return launch_tc<kEpiStore>(ma, mb, t, st);
-        case kEpiResidual: return launch_tc<kEpiResidual>(ma, mb, t, st);
-        case kEpiGluSilu: return launch_tc<kEpiGluSilu>(ma, mb, t, st);
-        case kEpiGluGelu: return launch_tc<kEpiGluGelu>(ma, mb, t, st);
-    }
-    return -1;
+    return int4 ? launch_epi<1>(ma, mb, t, epi, st) : launch_epi<0>(ma, mb, t, epi, st);
 }
 
 }  // namespace cb
