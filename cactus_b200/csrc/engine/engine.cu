@@ -260,6 +260,7 @@ void Engine::init(const std::string& folder, size_t context_size, size_t max_bat
     sink_ = 4;
     if (const char* w = std::getenv("CACTUS_KV_WINDOW_SIZE")) window_ = std::strtoul(w, nullptr, 10);
     if (const char* s = std::getenv("CACTUS_KV_SINK_SIZE")) sink_ = std::strtoul(s, nullptr, 10);
+    if (const char* f = std::getenv("CACTUS_B200_CAUSAL_FIX")) causal_fix_ = std::strtoul(f, nullptr, 10) != 0;
     if (cfg_.model_type == kGemma) window_ = 0, sink_ = 0;
     cap_ = std::max<size_t>(context_size, 1);
     if (const char* c = std::getenv("CACTUS_B200_KV_CAPACITY")) cap_ = std::max(cap_, (size_t)std::strtoul(c, nullptr, 10));
@@ -510,7 +511,8 @@ void Engine::forward(int B, int S, bool graph_mode) {
                     throw std::runtime_error("split attention launch failed");
                 ++launches_;
             } else if (launch_attention_hybrid_exact(q_, kcl, vcl, ksl, vsl, kl, vl, attn_, B, S, (int)cache_len_, S, Hq_,
-                                              Hkv_, D_, attention_scale_, (long long)total_len_, 1, 128,
+                                              Hkv_, D_, attention_scale_,
+                                              causal_fix_ ? (long long)cache_len_ : (long long)total_len_, 1, 128,
                                               cache_bstride_, scale_bstride_, stream_, ds) != 0)
                 throw std::runtime_error("unsupported head_dim for the hybrid attention kernel");
         }
@@ -973,6 +975,11 @@ CB_API int cactus_engine_reset(cactus_engine_t engine) {
 CB_API int cactus_engine_set_cache_window(cactus_engine_t engine, size_t window_size, size_t sink_size) {
     if (!engine) return CB_ERR_ARG;
     return guarded([&] { E(engine)->set_window(window_size, sink_size); });
+}
+
+CB_API int cactus_engine_set_causal_fix(cactus_engine_t engine, int on) {
+    if (!engine) return CB_ERR_ARG;
+    return guarded([&] { E(engine)->set_causal_fix(on != 0); });
 }
 
 CB_API int cactus_engine_info(cactus_engine_t engine, uint32_t* out8) {

@@ -50,6 +50,10 @@ public:
     ~Engine();
     void init(const std::string& folder, size_t context_size, size_t max_batch, int device);
     void reset();
+    // causal-correct masking inside a prefill chunk after the window has slid (off: the
+    // reference's behaviour, whose mask uses the total position and so lets a chunk's queries
+    // see its later keys once total > cache index; kernel_attention.cpp:331-346)
+    void set_causal_fix(bool on) { causal_fix_ = on; }
     void set_window(size_t w, size_t s) {
         if (cfg_.model_type == kGemma) return;  // Gemma keeps its cache unbounded
         if (w > cap_) throw std::runtime_error("window exceeds the KV cache capacity");
@@ -120,6 +124,7 @@ private:
     size_t window_ = 512, sink_ = 4, cap_ = 512;
     long long cache_bstride_ = 0, scale_bstride_ = 0;
     int seq0_ = 0;  // cache slot of sequence 0 of the current forward (per-sequence prefill)
+    bool causal_fix_ = false;
     int8_t *kc_ = nullptr, *vc_ = nullptr;
     float *ks_ = nullptr, *vs_ = nullptr;
     uint8_t* tmp_kv_ = nullptr;

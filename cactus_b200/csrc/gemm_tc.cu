@@ -9,18 +9,18 @@
 // one of four TMEM buffers, and the epilogue warps read the groups back in order and continue
 // the fp32 chains in registers while the tensor core fills the next buffers.
 //
-// CTA = 128 activation rows x 128 weight rows, 10 warps:
+// CTA = 128 activation rows x 128 weight rows, 6 warps:
 //   warp 0  producer: 2-D TMA tile loads (cp.async.bulk.tensor, 128-byte swizzle, no
 //           multicast) of the A and B K-chunks (128 bytes of K) into a 4-stage ring, and the
 //           chunk's fp16 group scales into a scale ring;
 //   warp 1  allocates TMEM (512 columns) and one thread issues the MMAs; tcgen05.commit
 //           signals TMEM buffers full and ring stages free;
-//   warps 2-9  epilogue: warp w reads TMEM lanes 32 * (w % 4) (its tile rows) and columns
-//           64 * ((w - 2) / 4) of each group buffer (tcgen05.ld), continues 64 fp32 chains
-//           per thread, then scales by As and writes fp16 (store / residual / GLU).
+//   warps 2-5  epilogue: warp w reads TMEM lanes 32 * (w % 4) (its tile rows) and all 128
+//           columns of each group buffer (tcgen05.ld), continues 128 fp32 chains per
+//           thread, then scales by As and writes fp16 (store / residual / GLU).
 // INT4 weights ([N, K/2] nibbles, low = even k): the producer loads the packed chunk with a
-// 1-D bulk copy and the MMA warp's partner lanes (warp 1, lanes 0-31) unpack it into the
-// swizzled int8 layout before the MMAs (sign-extended nibbles; the group sums are exact).
+// 2-D TMA tile and, one chunk behind its loads, unpacks it into the swizzled int8 layout
+// before the MMAs (sign-extended nibbles; the group sums are exact).
 // Every wait is bounded; a timeout raises the device error and every role leaves in order
 // (TMEM freed by its allocator after all warps meet).
 // This file is compiled as whole-program device code (build.py WHOLE_PROGRAM).
@@ -46,8 +46,14 @@ constexpr int kSStages = 8;                             // scale ring (one slot 
 constexpr int kSSlot = 4 * kBN * 4;                     // up to 4 groups x 128 columns, fp32
 constexpr int kTBufs = 4;                               // TMEM group buffers of 128 columns
 constexpr int kTmemCols = kTBufs * kBN;                 // 512
-constexpr int kWarps = 10, kThreads = kWarps * 32;
-constexpr int kEpiWarps = 8;
+// 6 warps: the 32-bit register file of each of the four SM sub-partitions (16K registers)
+// holds at most two of them at the 200-odd registers the epilogue needs (ten warps would cap
+// every thread at 168); four epilogue warps, one per TMEM lane quarter, own all 128 columns.
+constexpr int kWarps = 6, kThreads = kWarps * 32;
+constexpr int kEpiWarps = 4;
+constexpr int kCPT = kBN;          // columns per epilogue thread
+constexpr int kSW = 8;             // columns per TMEM read slice
+constexpr int kSL = kCPT / kSW;    // slices per group
 constexpr uint32_t kSpin = 1u << 24;
 
 struct TcArgs {
@@ -151,6 +157,19 @@ __device__ __forceinline__ void tmem_wait_ld(int (&v)[16]) {
                  : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld8_issue(uint32_t taddr, int (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld(int (&v)[8]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7])
+                 :
+                 : "memory");
+}
+
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, unsigned parity, volatile int* abort) {
     for (uint32_t i = 0; i < kSpin; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -182,7 +201,7 @@ __device__ __forceinline__ void unpack_chunk_int4(const uint8_t* packed, uint8_t
 }
 
 template <int EPI, int I4>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, TcArgs a) {
     pdl_launch_dependents();
     // Stage bases must be 1024-byte aligned for the swizzle atoms; the declared alignment of
@@ -306,11 +325,12 @@ __global__ void __maxnreg__(200)
         __syncwarp();
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int q = warp & 3, h = (warp - 2) >> 2;
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 64);
+        const int q = warp & 3;  // TMEM lane quarter of this warp (hardware rule: warp id % 4)
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
         // arm every group buffer with the bias (completion 0 of tempty)
         for (int b = 0; b < kTBufs; ++b) {
-            tmem_st64_bias(taddr + (uint32_t)(b * kBN));
+#pragma unroll
+            for (int c64 = 0; c64 < kCPT / 64; ++c64) tmem_st64_bias(taddr + (uint32_t)(b * kBN + c64 * 64));
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[b]);
@@ -318,39 +338,42 @@ __global__ void __maxnreg__(200)
         const float bias = 12582912.0f;
         const unsigned long long bias2 =
             ((unsigned long long)__float_as_uint(bias) << 32) | (unsigned long long)__float_as_uint(bias);
-        unsigned long long run[32];
+        unsigned long long run[kCPT / 2];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) run[j] = 0ull;  // two fp32 zeros
-        // Software-pipelined over the groups in slices of 16 columns: the TMEM read of the next
+        for (int j = 0; j < kCPT / 2; ++j) run[j] = 0ull;  // two fp32 zeros
+        // Software-pipelined over the groups in slices of kSW columns: the TMEM read of the next
         // slice is in flight while the current one runs through the chains.
-        auto chains = [&](const int (&v)[16], int grp, int sl) {
+        auto chains = [&](const int (&v)[kSW], int grp, int sl) {
             const int c = grp / gpc, gi = grp % gpc, ss = c % kSStages;
             const ulonglong2* sc =
-                reinterpret_cast<const ulonglong2*>(sscale + ss * (kSSlot / 4) + gi * kBN + h * 64 + sl * 16);
+                reinterpret_cast<const ulonglong2*>(sscale + ss * (kSSlot / 4) + gi * kBN + sl * kSW);
 #pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
+            for (int j4 = 0; j4 < kSW / 4; ++j4) {
                 const ulonglong2 sv = sc[j4];
-                chain2(run[sl * 8 + 2 * j4], v[4 * j4], v[4 * j4 + 1], sv.x, bias2);
-                chain2(run[sl * 8 + 2 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3], sv.y, bias2);
+                chain2(run[sl * (kSW / 2) + 2 * j4], v[4 * j4], v[4 * j4 + 1], sv.x, bias2);
+                chain2(run[sl * (kSW / 2) + 2 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3], sv.y, bias2);
             }
         };
-        // slice t = 4 * group + sl; before issuing the first slice of a group, wait until the
+        // slice t = kSL * group + sl; before issuing the first slice of a group, wait until the
         // group's buffer is full (and, for the first group of a chunk, its scales staged)
-        auto issue = [&](int t, int (&v)[16]) -> bool {
-            const int grp = t >> 2, sl = t & 3, b = grp % kTBufs;
+        auto issue = [&](int t, int (&v)[kSW]) -> bool {
+            const int grp = t / kSL, sl = t % kSL, b = grp % kTBufs;
             if (sl == 0) {
                 const int c = grp / gpc;
                 if (grp % gpc == 0 && !wait_or_abort(&sfull[c % kSStages], (c / kSStages) & 1, abort)) return false;
                 if (!wait_or_abort(&tfull[b], (grp / kTBufs) & 1, abort)) return false;
                 tc_fence_after();
             }
-            tmem_ld16_issue(taddr + (uint32_t)(b * kBN + sl * 16), v);
+            tmem_ld8_issue(taddr + (uint32_t)(b * kBN + sl * kSW), v);
             return true;
         };
         // after the last slice of a group: re-arm its buffer, hand it back, free the scale slot
         auto retire = [&](int grp) {
             const int b = grp % kTBufs;
-            if (grp + kTBufs < ngroups) tmem_st64_bias(taddr + (uint32_t)(b * kBN));
+            if (grp + kTBufs < ngroups) {
+#pragma unroll
+                for (int c64 = 0; c64 < kCPT / 64; ++c64) tmem_st64_bias(taddr + (uint32_t)(b * kBN + c64 * 64));
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[b]);
@@ -359,40 +382,36 @@ __global__ void __maxnreg__(200)
                 if (lane == 0) mbar_arrive(&sempty[(grp / gpc) % kSStages]);
             }
         };
-        const int T = ngroups * 4;
-        int x[16], y[16];
+        const int T = ngroups * kSL;
+        int x[kSW], y[kSW];
         bool ok = issue(0, x);
         for (int grp = 0; grp < ngroups && ok; ++grp) {
-            const int t = grp * 4;
-            tmem_wait_ld(x);
-            ok = issue(t + 1, y);
-            chains(x, grp, 0);
-            if (!ok) break;
-            tmem_wait_ld(y);
-            ok = issue(t + 2, x);
-            chains(y, grp, 1);
-            if (!ok) break;
-            tmem_wait_ld(x);
-            ok = issue(t + 3, y);
-            chains(x, grp, 2);
-            if (!ok) break;
-            tmem_wait_ld(y);
-            retire(grp);
-            if (t + 4 < T) ok = issue(t + 4, x);
-            chains(y, grp, 3);
+            const int t0 = grp * kSL;
+#pragma unroll
+            for (int sp = 0; sp < kSL; sp += 2) {
+                tmem_wait_ld(x);
+                ok = issue(t0 + sp + 1, y);
+                chains(x, grp, sp);
+                if (!ok) break;
+                tmem_wait_ld(y);
+                if (sp + 2 == kSL) retire(grp);
+                if (t0 + sp + 2 < T) ok = issue(t0 + sp + 2, x);
+                chains(y, grp, sp + 1);
+                if (!ok) break;
+            }
         }
         const int m = m0 + q * 32 + lane;
-        // column j of this thread's 64: lane (j & 1) of the pair run[j >> 1]
+        // column j of this thread's kCPT: lane (j & 1) of the pair run[j >> 1]
         auto col = [&](int j) -> float {
             return __uint_as_float((j & 1) ? (unsigned)(run[j >> 1] >> 32) : (unsigned)(run[j >> 1] & 0xFFFFFFFFull));
         };
         if (ok && !*abort && m < a.M) {
             const float asm_ = a.as[m];
-            const int nb = n0 + h * 64;
+            const int nb = n0;
             if constexpr (EPI == kEpiGluSilu || EPI == kEpiGluGelu) {
                 int4* o4 = reinterpret_cast<int4*>(a.out + (size_t)m * (a.N / 2) + nb / 2);
 #pragma unroll
-                for (int j8 = 0; j8 < 4; ++j8) {
+                for (int j8 = 0; j8 < kCPT / 16; ++j8) {
                     int4 ov;
                     __half* oh = reinterpret_cast<__half*>(&ov);
 #pragma unroll
@@ -408,7 +427,7 @@ __global__ void __maxnreg__(200)
                 int4* o4 = reinterpret_cast<int4*>(a.out + (size_t)m * a.N + nb);
                 const int4* r4 = reinterpret_cast<const int4*>(a.resid + (size_t)m * a.N + nb);
 #pragma unroll
-                for (int j8 = 0; j8 < 8; ++j8) {
+                for (int j8 = 0; j8 < kCPT / 8; ++j8) {
                     int4 ov;
                     __half* oh = reinterpret_cast<__half*>(&ov);
                     if constexpr (EPI == kEpiResidual) {

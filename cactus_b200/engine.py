@@ -45,6 +45,10 @@ class Engine:
     def set_cache_window(self, window: int, sink: int = 4):
         self._check(self._L.cactus_engine_set_cache_window(self.h, window, sink), "set_cache_window")
 
+    def set_causal_fix(self, on: bool = True):
+        """Causal-correct masking of prefill chunks after the window slid (off = reference)."""
+        self._check(self._L.cactus_engine_set_causal_fix(self.h, 1 if on else 0), "set_causal_fix")
+
     def prefill(self, tokens, chunk_size: int = 256):
         t = np.ascontiguousarray(tokens, np.uint32)
         self._check(self._L.cactus_engine_prefill(self.h, t.ctypes.data_as(C.c_void_p), t.size, chunk_size), "prefill")

@@ -37,6 +37,13 @@ CB_API const char* cactus_engine_last_error(void);
 CB_API int cactus_engine_reset(cactus_engine_t engine);
 /* Model::set_cache_window (engine.h:531); window 0 disables sliding */
 CB_API int cactus_engine_set_cache_window(cactus_engine_t engine, size_t window_size, size_t sink_size);
+/* Causal-correct masking of prefill chunks after the KV window has slid (on != 0). No
+ * reference counterpart: off (the default) is the reference's behaviour, where the mask of
+ * cactus_attention_hybrid_int8_fp16 uses the total position (kernel_attention.cpp:331-346 with
+ * engine_cache.cpp:111-120), so once total > cache index a chunk's queries also see the
+ * chunk's later keys; on masks by the cache index. Decode steps are the same in both modes.
+ * Also set by CACTUS_B200_CAUSAL_FIX=1 at creation. */
+CB_API int cactus_engine_set_causal_fix(cactus_engine_t engine, int on);
 /* model dimensions: out[0..7] = vocab, layers, hidden, heads, kv_heads, head_dim, ffn, model_type */
 CB_API int cactus_engine_info(cactus_engine_t engine, uint32_t* out8);
 

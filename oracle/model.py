@@ -129,7 +129,7 @@ class RefKVCache:
 
 
 class RefModel:
-    def __init__(self, folder, context_size=512, window=None, sink=4):
+    def __init__(self, folder, context_size=512, window=None, sink=4, causal_fix=False):
         self.cfg = c = read_config(folder)
         self.type = c["model_type"]
         rd = lambda n: read_weights(os.path.join(folder, n))
@@ -159,6 +159,9 @@ class RefModel:
             w, sink = 0, 0  # GemmaModel::post_init (model_gemma.cpp:17-19)
         self.kv = RefKVCache(c["num_layers"], self.Hkv, self.D, w, sink)
         self.last_logits = None
+        # causal-correct masking after the window slid (an option of the device engine, not
+        # of the reference: there the mask uses the total position)
+        self.causal_fix = causal_fix
 
     # ---- kernels on graph nodes
     def linear(self, x, w):
@@ -211,7 +214,7 @@ class RefModel:
             if self.kv.current > 0:
                 n = self.kv.current
                 attn = R.attention_hybrid(q4, self.kv.k[l][:n], self.kv.v[l][:n], self.kv.ks[l][:n],
-                                          self.kv.vs[l][:n], k4, v4, self.scale, pos)
+                                          self.kv.vs[l][:n], k4, v4, self.scale, n if self.causal_fix else pos)
             else:
                 win = 512 if (self.type == "gemma" and not self.is_global(l)) else 0
                 attn = R.attention(q4, k4, v4, self.scale, pos, win, True)

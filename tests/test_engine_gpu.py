@@ -77,6 +77,27 @@ def test_prefill_chunks_and_long_prompt(folders):
     eng.close()
 
 
+def test_causal_fix_mode_after_the_window_slid(folders):
+    """A 300-token prompt with window 128: the second prefill chunk runs after the cache slid,
+    where the reference's mask uses the total position (its queries see the chunk's later
+    keys). Default mode reproduces that; cactus_engine_set_causal_fix masks by the cache
+    index. Both match the restatement in the same mode, and the two modes differ."""
+    folder = folders["qwen"]
+    prompt = np.random.default_rng(13).integers(0, 1000, 300).tolist()
+    logits = {}
+    for fix in (False, True):
+        eng = Engine(folder, context_size=512)
+        eng.set_cache_window(128, 4)
+        eng.set_causal_fix(fix)
+        got = eng.generate_greedy(prompt, 8).tolist()
+        logits[fix] = eng.last_logits()
+        eng.close()
+        ref = OM.RefModel(folder, context_size=512, window=128, sink=4, causal_fix=fix)
+        assert got == ref.generate_greedy(prompt, 8)
+        assert _rel(logits[fix], ref.last_logits) <= TOL
+    assert not np.array_equal(logits[False].view(np.uint16), logits[True].view(np.uint16))
+
+
 def test_sliding_window_matches_oracle(folders):
     """Sink + sliding window cache (engine_cache.cpp:163-329) with window 16 and 4 sinks."""
     folder = folders["qwen"]
