@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
     const float* __restrict__ ks, const float* __restrict__ vs, const __half* __restrict__ Kn,
     const __half* __restrict__ Vn, __half* __restrict__ O, int S, int cache_len, int new_len, int Hq, int Hkv,
     float scale, long long pos_off, int causal, int qgs, long long kc_bstride, long long sc_bstride,
-    const int* __restrict__ dstate) {
+    const int* __restrict__ dstate, KvPaging pg) {
     pdl_launch_dependents();
     pdl_wait();
     if (dstate) {
@@ -285,10 +285,13 @@ __global__ void __launch_bounds__(256) attn_hybrid_exact_kernel(
 
     AttnCoreArgs c;
     c.qs = qs;
-    c.Kc = Kc + b * kc_bstride + (size_t)kvh * D;
-    c.Vc = Vc + b * kc_bstride + (size_t)kvh * D;
-    c.ks = ks + b * sc_bstride + (size_t)kvh * nqg;
-    c.vs = vs + b * sc_bstride + (size_t)kvh * nqg;
+    const long long kb = pg.table ? 0 : b * kc_bstride, sb = pg.table ? 0 : b * sc_bstride;
+    c.Kc = Kc + kb + (size_t)kvh * D;
+    c.Vc = Vc + kb + (size_t)kvh * D;
+    c.ks = ks + sb + (size_t)kvh * nqg;
+    c.vs = vs + sb + (size_t)kvh * nqg;
+    c.pages = pg.table ? pg.table + (size_t)b * pg.pps : nullptr;
+    c.page_shift = pg.shift;
     c.Kn = Kn + (size_t)b * new_len * kv_row + (size_t)kvh * D;
     c.Vn = Vn + (size_t)b * new_len * kv_row + (size_t)kvh * D;
     c.kv_row = (long long)kv_row;
@@ -317,7 +320,7 @@ int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_
                                   const float* vs, const __half* kn, const __half* vn, __half* o, int B, int S,
                                   int cache_len, int new_len, int Hq, int Hkv, int D, float scale, long long pos_off,
                                   int causal, int qgs, long long kc_bstride, long long sc_bstride, cudaStream_t st,
-                                  const int* dstate) {
+                                  const int* dstate, KvPaging pg) {
     const unsigned items = (unsigned)((long long)B * Hq * S);
     // long caches: the same arithmetic split over the keys (not while the lengths live on the
     // device or the stream is being captured: the split path sizes a scratch buffer on the host)
@@ -325,7 +328,7 @@ int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_
     if (!dstate && (long long)cache_len + new_len >= kSplitMinKeys && cudaStreamIsCapturing(st, &cap) == cudaSuccess &&
         cap == cudaStreamCaptureStatusNone &&
         launch_attention_split(q, kc, vc, ks, vs, kn, vn, o, B, S, cache_len, new_len, Hq, Hkv, D, scale, pos_off,
-                               causal, qgs, kc_bstride, sc_bstride, st) == 0)
+                               causal, qgs, kc_bstride, sc_bstride, st, pg) == 0)
         return 0;
 #define CB_EXACT(DD)                                                                                          \
     {                                                                                                         \
@@ -338,7 +341,7 @@ int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_
         }                                                                                                     \
         launch_k(attn_hybrid_exact_kernel<DD>, dim3(items), dim3(256), sm, st, q, kc, vc, ks, vs, kn, vn, o, S, cache_len,    \
                                                              new_len, Hq, Hkv, scale, pos_off, causal, qgs,    \
-                                                             kc_bstride, sc_bstride, dstate);                  \
+                                                             kc_bstride, sc_bstride, dstate, pg);              \
         return 0;                                                                                             \
     }
     if (qgs % 8 || (D + qgs - 1) / qgs > 2) return -1;

@@ -57,6 +57,8 @@ struct AttnCoreArgs {
     int causal;
     float scale;
     int prestaged;        // the caller already issued (and committed) chunk 0's cp.async copies
+    const int* pages = nullptr;  // paged cache: this sequence's page table (Kc/Vc/ks/vs = pool row 0)
+    int page_shift = 0;
 };
 
 // Issues the cp.async copies of the cached INT8 rows and scales of chunk [c0, c0 + CH) and
@@ -74,14 +76,16 @@ __device__ __forceinline__ void attn_stage_chunk(const AttnCoreArgs& a, uint8_t*
     const int ncached = (int)max(0LL, min((long long)n, (long long)a.cache_len - c0));
     for (int c = t; c < ncached * (D / 16); c += NT) {
         const int i = c / (D / 16), off = (c % (D / 16)) * 16;
-        const size_t src = (size_t)(c0 + i) * a.kv_row + off;
+        const long long row = a.pages ? kv_page_row(a.pages, a.page_shift, c0 + i) : c0 + i;
+        const size_t src = (size_t)row * a.kv_row + off;
         cp_async16(kraw + i * KR + off, a.Kc + src);
         cp_async16(vraw + i * D + off, a.Vc + src);
     }
     for (int c = t; c < ncached * nqg; c += NT) {
         const int i = c / nqg, g = c % nqg;
-        cp_async4(ksc + i * 2 + g, a.ks + (size_t)(c0 + i) * a.sc_row + g);
-        cp_async4(vsc + i * 2 + g, a.vs + (size_t)(c0 + i) * a.sc_row + g);
+        const long long row = a.pages ? kv_page_row(a.pages, a.page_shift, c0 + i) : c0 + i;
+        cp_async4(ksc + i * 2 + g, a.ks + (size_t)row * a.sc_row + g);
+        cp_async4(vsc + i * 2 + g, a.vs + (size_t)row * a.sc_row + g);
     }
     cp_async_commit();
 }

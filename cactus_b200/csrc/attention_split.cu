@@ -53,6 +53,7 @@ struct SplitArgs {
     int S, cache_len, new_len, Hq, Hkv, causal, qgs;
     float scale;
     const int* dstate;  // non-null: cache_len = dstate[0], pos_off = dstate[1] (read on the device)
+    KvPaging pg;        // paged cache (table non-null): kc/vc/ks/vs are the pools, no batch stride
 };
 
 // Lengths that live on the device (CUDA-graph decode): read after griddepcontrol.wait, since
@@ -114,15 +115,18 @@ __global__ void __launch_bounds__(kS1Threads) attn_split_scores_kernel(SplitArgs
     float* qs = ksc + kS1Keys * 2;                                  // [grp][D]
     float* sc = qs + grp * D;                                       // [grp][kS1Keys]
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const int8_t* Kc = a.kc + b * a.kc_bstride + (size_t)kvh * D;
-    const float* ks = a.ks + b * a.sc_bstride + (size_t)kvh * nqg;
+    const int* pt = a.pg.table ? a.pg.table + (size_t)b * a.pg.pps : nullptr;
+    const int8_t* Kc = a.kc + (pt ? 0 : b * a.kc_bstride) + (size_t)kvh * D;
+    const float* ks = a.ks + (pt ? 0 : b * a.sc_bstride) + (size_t)kvh * nqg;
     for (int c = t; c < ncached * (D / 16); c += kS1Threads) {
         const int i = c / (D / 16), off = (c % (D / 16)) * 16;
-        cp_async16(kraw + i * KR + off, Kc + (size_t)(c0 + i) * kv_row + off);
+        const long long row = pt ? kv_page_row(pt, a.pg.shift, c0 + i) : c0 + i;
+        cp_async16(kraw + i * KR + off, Kc + (size_t)row * kv_row + off);
     }
     for (int c = t; c < ncached * nqg; c += kS1Threads) {
         const int i = c / nqg, g = c % nqg;
-        cp_async4(ksc + i * 2 + g, ks + (size_t)(c0 + i) * sc_row + g);
+        const long long row = pt ? kv_page_row(pt, a.pg.shift, c0 + i) : c0 + i;
+        cp_async4(ksc + i * 2 + g, ks + (size_t)row * sc_row + g);
     }
     cp_async_commit();
     const int h0 = kvh * grp;
@@ -232,8 +236,9 @@ __global__ void __launch_bounds__(s2_dims<D>()) attn_split_chain_kernel(SplitArg
         }
         corr[j] = expf_cr(__fsub_rn(pm, bmx[j]));
     }
-    const int8_t* Vc = a.vc + b * a.kc_bstride + (size_t)kvh * D;
-    const float* vs = a.vs + b * a.sc_bstride + (size_t)kvh * nqg;
+    const int* pt = a.pg.table ? a.pg.table + (size_t)b * a.pg.pps : nullptr;
+    const int8_t* Vc = a.vc + (pt ? 0 : b * a.kc_bstride) + (size_t)kvh * D;
+    const float* vs = a.vs + (pt ? 0 : b * a.sc_bstride) + (size_t)kvh * nqg;
     const __half* Vn = a.vn + (size_t)b * a.new_len * kv_row + (size_t)kvh * D;
     const float* W = a.w + item * a.lw;
     const long long nch = (kv_end + kS2Keys - 1) / kS2Keys;
@@ -247,11 +252,13 @@ __global__ void __launch_bounds__(s2_dims<D>()) attn_split_chain_kernel(SplitArg
         const int ncached = (int)max(0LL, min((long long)n, (long long)a.cache_len - c0));
         for (int x = t; x < ncached * (DC / 16); x += DC) {
             const int i = x / (DC / 16), off = (x % (DC / 16)) * 16;
-            cp_async16(vraw + i * DC + off, Vc + (size_t)(c0 + i) * kv_row + dim0 + off);
+            const long long row = pt ? kv_page_row(pt, a.pg.shift, c0 + i) : c0 + i;
+            cp_async16(vraw + i * DC + off, Vc + (size_t)row * kv_row + dim0 + off);
         }
         for (int x = t; x < ncached * nqg; x += DC) {
             const int i = x / nqg, g = x % nqg;
-            cp_async4(vsc + g * kS2Keys + i, vs + (size_t)(c0 + i) * sc_row + g);
+            const long long row = pt ? kv_page_row(pt, a.pg.shift, c0 + i) : c0 + i;
+            cp_async4(vsc + g * kS2Keys + i, vs + (size_t)row * sc_row + g);
         }
         for (int x = t; x < n; x += DC) cp_async4(wst + x, W + c0 + x);
         cp_async_commit();
@@ -449,7 +456,7 @@ int split_common(const __half* q, const int8_t* kc, const int8_t* vc, const floa
                  const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len, int Hq,
                  int Hkv, int D, float scale, long long pos_off, int causal, int qgs, long long kc_bstride,
                  long long sc_bstride, long long size_keys, const int* dstate, float* scr, size_t scr_bytes,
-                 cudaStream_t st) {
+                 cudaStream_t st, KvPaging pg) {
     if (B < 1 || S < 1 || Hkv < 1 || Hq % Hkv || qgs % 8 || (D + qgs - 1) / qgs > 2) return -1;
     const long long lw = split_lw(size_keys);
     const long long nbw = lw / 32;
@@ -486,6 +493,7 @@ int split_common(const __half* q, const int8_t* kc, const int8_t* vc, const floa
     a.qgs = qgs;
     a.scale = scale;
     a.dstate = dstate;
+    a.pg = pg;
     switch (D) {
         case 64: return launch_split<64>(a, items, size_keys, B, st);
         case 128: return launch_split<128>(a, items, size_keys, B, st);
@@ -499,9 +507,9 @@ int split_common(const __half* q, const int8_t* kc, const int8_t* vc, const floa
 int launch_attention_split(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
                            const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len,
                            int Hq, int Hkv, int D, float scale, long long pos_off, int causal, int qgs,
-                           long long kc_bstride, long long sc_bstride, cudaStream_t st) {
+                           long long kc_bstride, long long sc_bstride, cudaStream_t st, KvPaging pg) {
     return split_common(q, kc, vc, ks, vs, kn, vn, o, B, S, cache_len, new_len, Hq, Hkv, D, scale, pos_off, causal,
-                        qgs, kc_bstride, sc_bstride, (long long)cache_len + new_len, nullptr, nullptr, 0, st);
+                        qgs, kc_bstride, sc_bstride, (long long)cache_len + new_len, nullptr, nullptr, 0, st, pg);
 }
 
 size_t attention_split_scratch_bytes(long long items, long long max_keys) {
@@ -529,10 +537,10 @@ int launch_attention_split_dev(const __half* q, const int8_t* kc, const int8_t* 
                                const __half* kn, const __half* vn, __half* o, int B, int S, int new_len, int Hq,
                                int Hkv, int D, float scale, int causal, int qgs, long long kc_bstride,
                                long long sc_bstride, long long max_keys, const int* dstate, float* scratch,
-                               size_t scratch_bytes, cudaStream_t st) {
+                               size_t scratch_bytes, cudaStream_t st, KvPaging pg) {
     if (!dstate || !scratch) return -1;
     return split_common(q, kc, vc, ks, vs, kn, vn, o, B, S, 0, new_len, Hq, Hkv, D, scale, 0, causal, qgs, kc_bstride,
-                        sc_bstride, max_keys, dstate, scratch, scratch_bytes, st);
+                        sc_bstride, max_keys, dstate, scratch, scratch_bytes, st, pg);
 }
 
 }  // namespace cb

@@ -14,9 +14,15 @@
 
 #include <utility>
 
+#include "kv_paging.h"
+
 namespace cb {
 
 constexpr int kNumSMs = 148;
+
+__host__ __device__ __forceinline__ long long kv_page_row(const int* seq_table, int shift, long long c) {
+    return ((long long)seq_table[c >> shift] << shift) + (c & ((1LL << shift) - 1));
+}
 
 // Device-side error word: kernels that give up a bounded wait record a code here and
 // return; the host reads it with cactus_cuda_device_error().

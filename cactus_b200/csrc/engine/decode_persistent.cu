@@ -427,6 +427,8 @@ __device__ __forceinline__ AttnCoreArgs attn_args(const PArgs& a, const PLayer& 
     c.causal = 1;
     c.scale = a.attn_scale;
     c.prestaged = 1;
+    c.pages = a.pages;
+    c.page_shift = a.page_shift;
     return c;
 }
 
@@ -503,8 +505,9 @@ __device__ __forceinline__ void attention_head(const PArgs& a, int l, int h, uin
         const int which = (warp - 2) / nqg, g = (warp - 2) % nqg;
         const int cnt = min(128, D - g * 128);
         const __half* src = (which ? hv : kr) + g * 128;
-        int8_t* dst = const_cast<int8_t*>(which ? c.Vc : c.Kc) + (size_t)cache_len * c.kv_row + g * 128;
-        float* sdst = const_cast<float*>(which ? c.vs : c.ks) + (size_t)cache_len * c.sc_row + g;
+        const long long row = c.pages ? kv_page_row(c.pages, c.page_shift, cache_len) : cache_len;
+        int8_t* dst = const_cast<int8_t*>(which ? c.Vc : c.Kc) + (size_t)row * c.kv_row + g * 128;
+        float* sdst = const_cast<float*>(which ? c.vs : c.ks) + (size_t)row * c.sc_row + g;
         kv_quant_group_warp(src, cnt, dst, sdst);
     }
     cbar();

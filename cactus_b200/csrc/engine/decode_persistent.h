@@ -41,6 +41,8 @@ struct PArgs {
     uint32_t* ring;         // optional: ring[state[2]] = next token
     int* state;             // [cache_len, total_len, step], advanced by the kernel
     PSync* sync;
+    const int* pages;       // paged KV cache: the sequence's page table (null: contiguous)
+    int page_shift;
     // filled by persistent_plan
     int slot_w, slot_s, nslots, kmax, gsm_ints, max_rows, work_bytes, attn_off;
 };

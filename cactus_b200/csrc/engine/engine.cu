@@ -176,6 +176,7 @@ Engine::~Engine() {
     if (stream_) cudaStreamDestroy(stream_);
     for (void* p : owned_) cudaFree(p);
     if (h_state_) cudaFreeHost(h_state_);
+    if (htable_) cudaFreeHost(htable_);
 }
 
 void Engine::init(const std::string& folder, size_t context_size, size_t max_batch, int device) {
@@ -267,8 +268,18 @@ void Engine::init(const std::string& folder, size_t context_size, size_t max_bat
     if (window_ > cap_) cap_ = window_;
 
     const int ng = (D_ + 127) / 128;
-    cache_bstride_ = (long long)cap_ * Hkv_ * D_;
-    scale_bstride_ = (long long)cap_ * Hkv_ * ng;
+    size_t cap_rows = cap_;
+    if (const char* pg = std::getenv("CACTUS_B200_KV_PAGE")) {
+        const long pt = std::strtol(pg, nullptr, 10);
+        if (pt > 0) {
+            if (pt < 16 || (pt & (pt - 1))) throw std::runtime_error("CACTUS_B200_KV_PAGE must be a power of two >= 16");
+            while ((1L << page_shift_) < pt) ++page_shift_;
+            pps_ = (int)((cap_ + pt - 1) / pt);
+            cap_rows = (size_t)pps_ * pt;  // a sequence slot's share of the pool, in rows
+        }
+    }
+    cache_bstride_ = (long long)cap_rows * Hkv_ * D_;
+    scale_bstride_ = (long long)cap_rows * Hkv_ * ng;
     const size_t cache_elems = (size_t)L_ * max_batch_ * cache_bstride_;
     const size_t scale_elems = (size_t)L_ * max_batch_ * scale_bstride_;
     kc_ = static_cast<int8_t*>(dmalloc(cache_elems, owned_));
@@ -276,6 +287,12 @@ void Engine::init(const std::string& folder, size_t context_size, size_t max_bat
     ks_ = static_cast<float*>(dmalloc(scale_elems * 4, owned_));
     vs_ = static_cast<float*>(dmalloc(scale_elems * 4, owned_));
     tmp_kv_ = static_cast<uint8_t*>(dmalloc((size_t)cache_bstride_ * 4 + 256, owned_));
+    if (page_shift_) {
+        dtable_ = static_cast<int*>(dmalloc((size_t)max_batch_ * pps_ * 4, owned_));
+        ck(cudaMallocHost(&htable_, (size_t)max_batch_ * pps_ * 4), "page table");
+        for (int i = 0; i < max_batch_ * pps_; ++i) htable_[i] = -1;
+        release_pages();
+    }
 
     const size_t R = (size_t)max_rows_;
     hidden_ = static_cast<__half*>(dmalloc(R * H_ * 2, owned_));
@@ -378,6 +395,8 @@ void Engine::setup_persistent() {
     a.tok_in = tok_in_;
     a.state = dstate_;
     a.sync = psync_;
+    a.pages = page_shift_ ? dtable_ : nullptr;  // sequence slot 0's table
+    a.page_shift = page_shift_;
     int sms = 0, optin = 0;
     ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_), "sm count");
     ck(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device_), "smem");
@@ -386,7 +405,42 @@ void Engine::setup_persistent() {
 
 bool Engine::is_global(int layer) const { return cfg_.model_type == kGemma && ((layer + 1) % 6) == 0; }
 
+// All pages back to the pool. Pages are handed out from the end of the pool first, so a
+// sequence's logical pages do not sit in physical order (the table is always exercised).
+void Engine::release_pages() {
+    if (!page_shift_) return;
+    free_pages_.resize((size_t)max_batch_ * pps_);
+    for (size_t i = 0; i < free_pages_.size(); ++i) free_pages_[i] = (int)i;
+    seq_pages_.assign(max_batch_, 0);
+}
+
+// Gives sequence slots [seq0, seq0 + B) pages for `rows` logical rows and uploads the table
+// when it changed. The host mirror is only rewritten after the stream has drained, so a copy
+// still queued never sees a later edit.
+void Engine::ensure_pages(int seq0, int B, size_t rows) {
+    if (!page_shift_) return;
+    const int need = (int)((rows + ((size_t)1 << page_shift_) - 1) >> page_shift_);
+    if (need > pps_) throw std::runtime_error("KV cache capacity exceeded");
+    bool synced = false, changed = false;
+    for (int b = seq0; b < seq0 + B; ++b) {
+        while (seq_pages_[b] < need) {
+            if (free_pages_.empty()) throw std::runtime_error("KV page pool exhausted");
+            if (!synced) {
+                ck(cudaStreamSynchronize(stream_), "page table");
+                synced = true;
+            }
+            htable_[(size_t)b * pps_ + seq_pages_[b]++] = free_pages_.back();
+            free_pages_.pop_back();
+            changed = true;
+        }
+    }
+    if (changed)
+        ck(cudaMemcpyAsync(dtable_, htable_, (size_t)max_batch_ * pps_ * 4, cudaMemcpyHostToDevice, stream_),
+           "page table");
+}
+
 void Engine::reset() {
+    release_pages();
     seq0_ = 0;
     cache_len_ = 0;
     total_len_ = 0;
@@ -468,10 +522,12 @@ void Engine::forward(int B, int S, bool graph_mode) {
         const LayerW& lw = layers_[l];
         __half* kl = kall_ + (size_t)l * kv_rows_stride;
         __half* vl = vall_ + (size_t)l * kv_rows_stride;
-        int8_t* kcl = kc_ + ((size_t)l * max_batch_ + seq0_) * cache_bstride_;
-        int8_t* vcl = vc_ + ((size_t)l * max_batch_ + seq0_) * cache_bstride_;
-        float* ksl = ks_ + ((size_t)l * max_batch_ + seq0_) * scale_bstride_;
-        float* vsl = vs_ + ((size_t)l * max_batch_ + seq0_) * scale_bstride_;
+        // contiguous: sequence seq0_'s slot; paged: the layer's pool (rows through the table)
+        const size_t slot = page_shift_ ? 0 : (size_t)seq0_;
+        int8_t* kcl = kc_ + ((size_t)l * max_batch_ + slot) * cache_bstride_;
+        int8_t* vcl = vc_ + ((size_t)l * max_batch_ + slot) * cache_bstride_;
+        float* ksl = ks_ + ((size_t)l * max_batch_ + slot) * scale_bstride_;
+        float* vsl = vs_ + ((size_t)l * max_batch_ + slot) * scale_bstride_;
 
         gemv(lw.qkv, kProRmsNormQuant, kEpiStore, hidden_, lw.in_norm, qkv_, nullptr, rows);
         QkvPostArgs qa = {};
@@ -507,13 +563,14 @@ void Engine::forward(int B, int S, bool graph_mode) {
             if (graph_mode && split_graph_ && S == 1) {
                 if (launch_attention_split_dev(q_, kcl, vcl, ksl, vsl, kl, vl, attn_, B, S, S, Hq_, Hkv_, D_,
                                                attention_scale_, 1, 128, cache_bstride_, scale_bstride_,
-                                               (long long)cap_ + 1, ds, split_scr_, split_scr_bytes_, stream_) != 0)
+                                               (long long)cap_ + 1, ds, split_scr_, split_scr_bytes_, stream_,
+                                               paging(seq0_)) != 0)
                     throw std::runtime_error("split attention launch failed");
                 ++launches_;
             } else if (launch_attention_hybrid_exact(q_, kcl, vcl, ksl, vsl, kl, vl, attn_, B, S, (int)cache_len_, S, Hq_,
                                               Hkv_, D_, attention_scale_,
                                               causal_fix_ ? (long long)cache_len_ : (long long)total_len_, 1, 128,
-                                              cache_bstride_, scale_bstride_, stream_, ds) != 0)
+                                              cache_bstride_, scale_bstride_, stream_, ds, paging(seq0_)) != 0)
                 throw std::runtime_error("unsupported head_dim for the hybrid attention kernel");
         }
         ck(cudaGetLastError(), "attention launch");
@@ -556,6 +613,7 @@ void Engine::update_kv(int l, int B, int S, const __half* kl, const __half* vl, 
     a.Hkv = Hkv_;
     a.D = D_;
     a.G = 128;
+    a.pg = paging(seq0_);
     if (graph_mode) {  // non-sliding append at cache_len (checked by the caller)
         a.src_tok0 = 0;
         a.ntok = S;
@@ -594,7 +652,25 @@ void Engine::update_kv(int l, int B, int S, const __half* kl, const __half* vl, 
     const size_t old = cache_len_;
     if (tts > 0 && old > sink_) {
         const long long shift_src = (long long)old - tts;
-        if (shift_src > (long long)sink_) {
+        if (shift_src > (long long)sink_ && page_shift_) {
+            for (int b = 0; b < B; ++b) {
+                KvMoveArgs mv = {};
+                mv.k_cache = kcl;
+                mv.v_cache = vcl;
+                mv.k_scales = ksl;
+                mv.v_scales = vsl;
+                mv.tmp = tmp_kv_;
+                mv.pg = paging(seq0_);
+                mv.b = b;
+                mv.Hkv = Hkv_;
+                mv.D = D_;
+                mv.ng = ng;
+                mv.src0 = shift_src;
+                mv.dst0 = (long long)sink_;
+                mv.n = tts;
+                launch_kv_move_paged(mv, stream_);
+            }
+        } else if (shift_src > (long long)sink_) {
             for (int b = 0; b < B; ++b) {
                 for (int which = 0; which < 2; ++which) {
                     int8_t* c = (which ? vcl : kcl) + (size_t)b * cache_bstride_;
@@ -660,6 +736,8 @@ void Engine::run_forward_tokens(const uint32_t* tokens, int B, int S) {
     if (B * S > max_rows_) throw std::runtime_error("too many rows for the engine buffers");
     if (cache_len_ + S > cap_) throw std::runtime_error("KV cache capacity exceeded");
     check_tokens(tokens, (size_t)B * S);
+    // rows this forward writes: the cache grows to cache_len + S, or to the window once it slides
+    ensure_pages(seq0_, B, window_ > 0 ? std::min(cache_len_ + S, window_) : cache_len_ + S);
     ck(cudaMemcpyAsync(ids_, tokens, (size_t)B * S * 4, cudaMemcpyHostToDevice, stream_), "ids");
     embed(ids_, B * S, hidden_);
     forward(B, S, false);
@@ -818,6 +896,9 @@ void Engine::generate(const uint32_t* prompts, int B, size_t P, size_t max_new, 
     push_state(0);
     const bool no_slide = cache_len_ > 0 && (window_ == 0 || cache_len_ + max_new <= window_) &&
                           cache_len_ + max_new <= cap_;
+    // pages for every row the decode steps write (the device-side decode paths append rows
+    // without returning to the host)
+    ensure_pages(0, B, window_ > 0 ? std::min(cache_len_ + max_new, window_) : std::min(cache_len_ + max_new, cap_));
     const bool can_graph = use_graph_ && no_slide;
     const bool can_persist = use_persistent_ && pplan_.ok && no_slide && B == 1;
     size_t step = 0;
@@ -913,6 +994,20 @@ void Engine::read_kv(size_t layer, int8_t* k, int8_t* v, float* ks, float* vs) {
     const int ng = (D_ + 127) / 128;
     const size_t nb = cache_len_ * Hkv_ * D_, ns = cache_len_ * Hkv_ * ng;
     const size_t lo = layer * max_batch_;
+    if (page_shift_) {  // sequence 0's rows, page by page through the table
+        const size_t P = (size_t)1 << page_shift_, rb = (size_t)Hkv_ * D_, rs = (size_t)Hkv_ * ng;
+        for (size_t r0 = 0; r0 < cache_len_; r0 += P) {
+            const size_t n = std::min(P, cache_len_ - r0), pr = (size_t)htable_[r0 >> page_shift_] << page_shift_;
+            ck(cudaMemcpyAsync(k + r0 * rb, kc_ + lo * cache_bstride_ + pr * rb, n * rb, cudaMemcpyDeviceToHost, stream_), "kv");
+            ck(cudaMemcpyAsync(v + r0 * rb, vc_ + lo * cache_bstride_ + pr * rb, n * rb, cudaMemcpyDeviceToHost, stream_), "kv");
+            ck(cudaMemcpyAsync(ks + r0 * rs, ks_ + lo * scale_bstride_ + pr * rs, n * rs * 4, cudaMemcpyDeviceToHost,
+                               stream_), "kv");
+            ck(cudaMemcpyAsync(vs + r0 * rs, vs_ + lo * scale_bstride_ + pr * rs, n * rs * 4, cudaMemcpyDeviceToHost,
+                               stream_), "kv");
+        }
+        ck(cudaStreamSynchronize(stream_), "read kv");
+        return;
+    }
     ck(cudaMemcpyAsync(k, kc_ + lo * cache_bstride_, nb, cudaMemcpyDeviceToHost, stream_), "kv");
     ck(cudaMemcpyAsync(v, vc_ + lo * cache_bstride_, nb, cudaMemcpyDeviceToHost, stream_), "kv");
     ck(cudaMemcpyAsync(ks, ks_ + lo * scale_bstride_, ns * 4, cudaMemcpyDeviceToHost, stream_), "kv");

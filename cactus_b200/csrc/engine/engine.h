@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "decode_persistent.h"
+#include "../kv_paging.h"
 #include "weights_io.h"
 
 namespace cb {
@@ -125,6 +126,25 @@ private:
     long long cache_bstride_ = 0, scale_bstride_ = 0;
     int seq0_ = 0;  // cache slot of sequence 0 of the current forward (per-sequence prefill)
     bool causal_fix_ = false;
+    // paged KV cache (CACTUS_B200_KV_PAGE = tokens per page, a power of two; 0 = contiguous):
+    // each layer's cache is a pool of pages, sequences own pages through a block table that
+    // every cache access (attention, append, window compaction) goes through
+    int page_shift_ = 0, pps_ = 0;
+    int* dtable_ = nullptr;         // device [max_batch, pps]
+    int* htable_ = nullptr;         // pinned host mirror
+    std::vector<int> free_pages_;
+    std::vector<int> seq_pages_;    // pages held by each sequence slot
+    KvPaging paging(int seq) const {
+        KvPaging p;
+        if (page_shift_) {
+            p.table = dtable_ + (size_t)seq * pps_;
+            p.shift = page_shift_;
+            p.pps = pps_;
+        }
+        return p;
+    }
+    void release_pages();
+    void ensure_pages(int seq0, int B, size_t rows);
     int8_t *kc_ = nullptr, *vc_ = nullptr;
     float *ks_ = nullptr, *vs_ = nullptr;
     uint8_t* tmp_kv_ = nullptr;

@@ -63,12 +63,37 @@ __global__ void kv_append_kernel(KvAppendArgs a) {
     for (int which = 0; which < 2; ++which) {
         const __half* src = (which ? a.v_new : a.k_new) +
                             (((size_t)b * a.S + a.src_tok0 + t) * a.Hkv + h) * a.D + g0;
-        int8_t* dst = (which ? a.v_cache : a.k_cache) + (size_t)b * a.cache_bstride +
-                      ((size_t)(dst0 + t) * a.Hkv + h) * a.D + g0;
-        float* sdst = (which ? a.v_scales : a.k_scales) + (size_t)b * a.scale_bstride +
-                      ((size_t)(dst0 + t) * a.Hkv + h) * ng + g;
+        // contiguous: sequence b's rows at its stride; paged: the physical row of its table
+        const long long row = a.pg.table ? kv_page_row(a.pg.table + (size_t)b * a.pg.pps, a.pg.shift, dst0 + t)
+                                         : dst0 + t;
+        const size_t kb = a.pg.table ? 0 : (size_t)b * a.cache_bstride;
+        const size_t sb = a.pg.table ? 0 : (size_t)b * a.scale_bstride;
+        int8_t* dst = (which ? a.v_cache : a.k_cache) + kb + ((size_t)row * a.Hkv + h) * a.D + g0;
+        float* sdst = (which ? a.v_scales : a.k_scales) + sb + ((size_t)row * a.Hkv + h) * ng + g;
         kv_quant_group_warp(src, cnt, dst, sdst);
     }
+}
+
+// paged compaction: phase 0 gathers the source rows (keys, values, scales) into tmp, phase 1
+// scatters them to the destination rows; one thread per 4-byte word
+__global__ void kv_move_paged_kernel(KvMoveArgs a, int phase) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const long long rb = (long long)a.Hkv * a.D / 4, rs = (long long)a.Hkv * a.ng;  // words per row
+    const long long per = 2 * rb + 2 * rs;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.n * per) return;
+    const long long r = i / per, w = i % per;
+    const int* tb = a.pg.table + (size_t)a.b * a.pg.pps;
+    const long long row = kv_page_row(tb, a.pg.shift, (phase == 0 ? a.src0 : a.dst0) + r);
+    uint32_t* slot;
+    if (w < rb) slot = reinterpret_cast<uint32_t*>(a.k_cache) + row * rb + w;
+    else if (w < 2 * rb) slot = reinterpret_cast<uint32_t*>(a.v_cache) + row * rb + (w - rb);
+    else if (w < 2 * rb + rs) slot = reinterpret_cast<uint32_t*>(a.k_scales) + row * rs + (w - 2 * rb);
+    else slot = reinterpret_cast<uint32_t*>(a.v_scales) + row * rs + (w - 2 * rb - rs);
+    uint32_t* t = reinterpret_cast<uint32_t*>(a.tmp) + i;
+    if (phase == 0) *t = *slot;
+    else *slot = *t;
 }
 
 // byte copy used for the sliding-window compaction (through a temporary, so overlap is safe)
@@ -201,6 +226,12 @@ void launch_kv_append(const KvAppendArgs& a, cudaStream_t st) {
     const int ng = (a.D + a.G - 1) / a.G;
     const long long warps = (long long)a.B * a.ntok * a.Hkv * ng;
     if (warps > 0) launch_k(kv_append_kernel, dim3(nb(warps * 32, 256)), dim3(256), 0, st, a);
+}
+void launch_kv_move_paged(const KvMoveArgs& a, cudaStream_t st) {
+    const long long words = a.n * (2LL * a.Hkv * a.D / 4 + 2LL * a.Hkv * a.ng);
+    if (words <= 0) return;
+    launch_k(kv_move_paged_kernel, dim3(nb(words, 256)), dim3(256), 0, st, a, 0);
+    launch_k(kv_move_paged_kernel, dim3(nb(words, 256)), dim3(256), 0, st, a, 1);
 }
 void launch_copy_bytes(void* dst, const void* src, long long n, cudaStream_t st) {
     if (n > 0)

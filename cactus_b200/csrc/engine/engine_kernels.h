@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../kv_paging.h"
+
 namespace cb {
 namespace eng {
 
@@ -36,7 +38,21 @@ struct KvAppendArgs {
     int src_tok0, ntok;
     long long dst0;
     const int* dstate;  // dst0 = cache_len when set
+    KvPaging pg;        // paged cache: caches / scales are the pools, rows through the table
 };
+// Sliding-window compaction of a paged cache: logical rows [src0, src0 + n) of sequence b
+// move to [dst0, dst0 + n) (through `tmp`, so the ranges may overlap); keys, values and scales.
+struct KvMoveArgs {
+    int8_t* k_cache;
+    int8_t* v_cache;
+    float* k_scales;
+    float* v_scales;
+    uint8_t* tmp;  // n * row bytes * 2 + n * scale bytes * 2
+    KvPaging pg;
+    int b, Hkv, D, ng;
+    long long src0, dst0, n;
+};
+void launch_kv_move_paged(const KvMoveArgs& a, cudaStream_t st);
 void launch_kv_append(const KvAppendArgs& a, cudaStream_t st);
 void launch_copy_bytes(void* dst, const void* src, long long n, cudaStream_t st);
 void launch_state_advance(int* state, int ntok, cudaStream_t st);

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "kv_paging.h"
+
 namespace cb {
 
 // ---- grouped GEMV (gemv.cu)
@@ -72,7 +74,7 @@ int launch_attention_hybrid_exact(const __half* q, const int8_t* kc, const int8_
                                   const float* vs, const __half* kn, const __half* vn, __half* o, int B, int S,
                                   int cache_len, int new_len, int Hq, int Hkv, int D, float scale, long long pos_off,
                                   int causal, int qgs, long long kc_bstride, long long sc_bstride, cudaStream_t st,
-                                  const int* dstate = nullptr);
+                                  const int* dstate = nullptr, KvPaging pg = KvPaging());
 void attention_prepare();  // kernel attributes, called before any graph capture
 // Exact hybrid attention split over the keys for long caches (attention_split.cu): same
 // result bits as launch_attention_hybrid_exact; -1 when the shape or the scratch size is
@@ -83,7 +85,7 @@ constexpr size_t kSplitMaxScratch = size_t(4) << 30;
 int launch_attention_split(const __half* q, const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
                            const __half* kn, const __half* vn, __half* o, int B, int S, int cache_len, int new_len,
                            int Hq, int Hkv, int D, float scale, long long pos_off, int causal, int qgs,
-                           long long kc_bstride, long long sc_bstride, cudaStream_t st);
+                           long long kc_bstride, long long sc_bstride, cudaStream_t st, KvPaging pg = KvPaging());
 // The same split with the lengths read on the device from dstate = [cache_len, total_len]
 // (CUDA-graph decode: one captured launch serves every step). The grid and the caller-owned
 // scratch (attention_split_scratch_bytes(B*S*Hq, max_keys) bytes) are sized for max_keys keys;
@@ -95,7 +97,7 @@ int launch_attention_split_dev(const __half* q, const int8_t* kc, const int8_t* 
                                const __half* kn, const __half* vn, __half* o, int B, int S, int new_len, int Hq,
                                int Hkv, int D, float scale, int causal, int qgs, long long kc_bstride,
                                long long sc_bstride, long long max_keys, const int* dstate, float* scratch,
-                               size_t scratch_bytes, cudaStream_t st);
+                               size_t scratch_bytes, cudaStream_t st, KvPaging pg = KvPaging());
 
 // ---- sampling (sample.cu)
 int launch_sample(const __half* logits, int V, float temperature, float top_p, int top_k, float uniform,
