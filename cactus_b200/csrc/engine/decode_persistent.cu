@@ -80,8 +80,9 @@ __host__ __device__ inline int rows_per_slot(int slot_w, int K) { return (slot_w
 
 // Bounded mbarrier wait with back-off: a thread spinning on try_wait keeps the SM's shared
 // memory pipe busy and slows every other warp of the block, so failed polls sleep `ns`.
-__device__ __forceinline__ bool wait_abortable(uint64_t* bar, unsigned par, const unsigned* abort, unsigned ns) {
-    for (uint32_t i = 0; i < (1u << 22); ++i) {
+__device__ __forceinline__ bool wait_abortable(uint64_t* bar, unsigned par, const unsigned* abort, unsigned ns,
+                                               unsigned limit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, par)) return true;
         __nanosleep(ns);
         if ((i & 15) == 15 && ld_volatile_u32(abort)) return false;
@@ -108,7 +109,7 @@ __device__ void producer(const PArgs& a, uint8_t* ring, uint64_t* full, uint64_t
         const int spr = rows_per_slot(a.slot_w, jw.K), ng = jw.K / a.G;
         for (int r = r0; r < r1; r += spr) {
             const int s = (int)(k % NS);
-            if (k >= (unsigned)NS && !wait_abortable(&empty[s], ((k / NS) - 1) & 1, &a.sync->abort, 256)) {
+            if (k >= (unsigned)NS && !wait_abortable(&empty[s], ((k / NS) - 1) & 1, &a.sync->abort, 256, a.spin_limit)) {
                 ok = false;
                 break;
             }
@@ -302,7 +303,7 @@ __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const C
         // the residual row of this thread's output, read before the slot wait (the hidden
         // state is stable since the last grid barrier)
         const __half res = (epi == kEpiResid && tid < rows) ? __ldcg(out + r + tid) : __float2half_rn(0.0f);
-        if (tid == 0) *m.flag = wait_abortable(&full[s], par, &a.sync->abort, 32) ? 1 : 0;
+        if (tid == 0) *m.flag = wait_abortable(&full[s], par, &a.sync->abort, 32, a.spin_limit) ? 1 : 0;
         cbar();
         if (!*m.flag) {
             if (tid == 0) set_abort(a, kDevTmaTimeout);
@@ -389,7 +390,7 @@ __device__ __forceinline__ bool grid_sync(const PArgs& a, unsigned& tgt, int* fl
             // on B200 with 148 blocks: 1.40 us per barrier against 1.78 us for relaxed polling
             // plus one acquire fence)
             while (ld_acquire_gpu(&a.sync->bar) < target) {
-                if (++i > (1u << 22) || ((i & 63) == 0 && ld_volatile_u32(&a.sync->abort))) {
+                if (++i > a.spin_limit || ((i & 63) == 0 && ld_volatile_u32(&a.sync->abort))) {
                     ok = false;
                     break;
                 }

@@ -43,6 +43,7 @@ struct PArgs {
     PSync* sync;
     const int* pages;       // paged KV cache: the sequence's page table (null: contiguous)
     int page_shift;
+    unsigned spin_limit;    // polls before a wait gives up (2^22; CACTUS_B200_SPIN_LIMIT lowers it in tests)
     // filled by persistent_plan
     int slot_w, slot_s, nslots, kmax, gsm_ints, max_rows, work_bytes, attn_off;
 };

@@ -396,6 +396,8 @@ void Engine::setup_persistent() {
     a.state = dstate_;
     a.sync = psync_;
     a.pages = page_shift_ ? dtable_ : nullptr;  // sequence slot 0's table
+    a.spin_limit = 1u << 22;
+    if (const char* e = std::getenv("CACTUS_B200_SPIN_LIMIT")) a.spin_limit = (unsigned)std::max(1L, std::strtol(e, nullptr, 10));
     a.page_shift = page_shift_;
     int sms = 0, optin = 0;
     ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_), "sm count");

@@ -210,15 +210,18 @@ int launch_one(const GemmArgs& g, cudaStream_t st) {
 }
 }  // namespace
 
-// The tcgen05 GEMM (gemm_tc.cu: TMA-fed tcgen05.mma, TMEM group accumulators) takes every
-// INT8 shape it supports; CACTUS_B200_GEMM=mma keeps this file's mma.sync kernel instead
-// (read once per process).
-bool gemm_tc_enabled() {
-    static const bool on = [] {
+// The tcgen05 GEMM (gemm_tc.cu: TMA-fed tcgen05.mma, TMEM group accumulators) takes the INT8 /
+// INT4 shapes it supports that fill at least one wave of its tiles; CACTUS_B200_GEMM=mma keeps
+// this file's mma.sync kernel for every shape, CACTUS_B200_GEMM=tc gives the tcgen05 kernel
+// every shape it supports (read once per process).
+int gemm_tc_mode() {
+    static const int mode = [] {
         const char* e = std::getenv("CACTUS_B200_GEMM");
-        return !(e && std::string(e) == "mma");
+        if (e && std::string(e) == "mma") return 0;
+        if (e && std::string(e) == "tc") return 2;
+        return 1;
     }();
-    return on;
+    return mode;
 }
 
 const char* gemm_check(int M, int K, int N, int G, int int4) {
@@ -229,14 +232,15 @@ const char* gemm_check(int M, int K, int N, int G, int int4) {
     return nullptr;
 }
 
-bool gemm_tc_ok(int M, int K, int N, int G, int int4);
+bool gemm_tc_ok(int M, int K, int N, int G, int int4, bool any_size);
 int launch_gemm_tc(const int8_t* aq, const float* as, const void* w, const __half* ws, __half* out,
                    const __half* resid, int M, int K, int N, int G, int int4, int epi, cudaStream_t st);
 
 int launch_gemm(const int8_t* aq, const float* as, const void* w, const __half* ws, __half* out, const __half* resid,
                 int M, int K, int N, int G, int int4, int epi, cudaStream_t st) {
     if (gemm_check(M, K, N, G, int4)) return -1;
-    if (gemm_tc_enabled() && gemm_tc_ok(M, K, N, G, int4)) {
+    const int mode = gemm_tc_mode();
+    if (mode != 0 && gemm_tc_ok(M, K, N, G, int4, mode == 2)) {
         const int rc = launch_gemm_tc(aq, as, w, ws, out, resid, M, K, N, G, int4, epi, st);
         if (rc != -2) return rc;  // -2: operands not addressable by a tensor map; mma.sync below
     }

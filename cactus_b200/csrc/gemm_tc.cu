@@ -9,15 +9,15 @@
 // one of four TMEM buffers, and the epilogue warps read the groups back in order and continue
 // the fp32 chains in registers while the tensor core fills the next buffers.
 //
-// CTA = 128 activation rows x 128 weight rows, 6 warps:
+// CTA = 128 activation rows x 128 weight rows, 10 warps:
 //   warp 0  producer: 2-D TMA tile loads (cp.async.bulk.tensor, 128-byte swizzle, no
 //           multicast) of the A and B K-chunks (128 bytes of K) into a 4-stage ring, and the
 //           chunk's fp16 group scales into a scale ring;
 //   warp 1  allocates TMEM (512 columns) and one thread issues the MMAs; tcgen05.commit
 //           signals TMEM buffers full and ring stages free;
-//   warps 2-5  epilogue: warp w reads TMEM lanes 32 * (w % 4) (its tile rows) and all 128
-//           columns of each group buffer (tcgen05.ld), continues 128 fp32 chains per
-//           thread, then scales by As and writes fp16 (store / residual / GLU).
+//   warps 2-9  epilogue: warp w reads TMEM lanes 32 * (w % 4) (its tile rows) and columns
+//           64 * ((w - 2) / 4) of each group buffer (tcgen05.ld), continues 64 fp32 chains
+//           per thread, then scales by As and writes fp16 (store / residual / GLU).
 // INT4 weights ([N, K/2] nibbles, low = even k): the producer loads the packed chunk with a
 // 2-D TMA tile and, one chunk behind its loads, unpacks it into the swizzled int8 layout
 // before the MMAs (sign-extended nibbles; the group sums are exact).
@@ -46,14 +46,12 @@ constexpr int kSStages = 8;                             // scale ring (one slot 
 constexpr int kSSlot = 4 * kBN * 4;                     // up to 4 groups x 128 columns, fp32
 constexpr int kTBufs = 4;                               // TMEM group buffers of 128 columns
 constexpr int kTmemCols = kTBufs * kBN;                 // 512
-// 6 warps: the 32-bit register file of each of the four SM sub-partitions (16K registers)
-// holds at most two of them at the 200-odd registers the epilogue needs (ten warps would cap
-// every thread at 168); four epilogue warps, one per TMEM lane quarter, own all 128 columns.
-constexpr int kWarps = 6, kThreads = kWarps * 32;
-constexpr int kEpiWarps = 4;
-constexpr int kCPT = kBN;          // columns per epilogue thread
-constexpr int kSW = 8;             // columns per TMEM read slice
-constexpr int kSL = kCPT / kSW;    // slices per group
+// 10 warps: eight epilogue warps, two per TMEM lane quarter, each owning 64 columns. (Ten
+// warps leave at most 168 registers a thread, since each SM sub-partition's 16K registers
+// must hold three of them; the epilogue stays below that.)
+constexpr int kWarps = 10, kThreads = kWarps * 32;
+constexpr int kEpiWarps = 8;
+constexpr int kCPT = kBN / 2;      // columns per epilogue thread
 constexpr uint32_t kSpin = 1u << 24;
 
 struct TcArgs {
@@ -110,17 +108,18 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     return p;
 }
 
-// 64 TMEM columns of the warp's 32 lanes set to the integer kBias (a store and its wait)
+// 64 TMEM columns of the warp's 32 lanes set to the integer 0x4B400000 (the store is
+// asynchronous: tmem_wait_st before the columns are handed to the tensor core)
 __device__ __forceinline__ void tmem_st64_bias(uint32_t taddr) {
     const int b = 0x4B400000;
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
         "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};\n\t"
-        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
         "r"(b)
         : "memory");
 }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Two lanes of the fp32 group chain: run = fma(float(gsum), scale, run) for a pair of columns,
 // with one f32x2 subtract and one f32x2 fused multiply-add (each lane rounded as the scalar
@@ -137,37 +136,19 @@ __device__ __forceinline__ void chain2(unsigned long long& run, int v0, int v1, 
         : "r"(v0), "r"(v1), "l"(s2), "l"(bias2));
 }
 
-// one warp: 16 consecutive TMEM columns of its 32 lanes, issued without waiting; the values
-// are valid after tmem_wait_ld on the same array, whose register operands keep every use of
-// them behind the wait
-__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, int (&v)[16]) {
+// one warp: 32 consecutive TMEM columns of its 32 lanes; load and wait in one statement (a
+// separate wait would let the compiler schedule uses of the registers ahead of it)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
         : "r"(taddr)
         : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld(int (&v)[16]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
-                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
-                   "+r"(v[15])
-                 :
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld8_issue(uint32_t taddr, int (&v)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-                 : "r"(taddr)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld(int (&v)[8]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7])
-                 :
-                 : "memory");
 }
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, unsigned parity, volatile int* abort) {
@@ -325,79 +306,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int q = warp & 3;  // TMEM lane quarter of this warp (hardware rule: warp id % 4)
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+        const int q = warp & 3, h = (warp - 2) >> 2;  // TMEM lane quarter (warp id % 4), column half
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * kCPT);
         // arm every group buffer with the bias (completion 0 of tempty)
-        for (int b = 0; b < kTBufs; ++b) {
-#pragma unroll
-            for (int c64 = 0; c64 < kCPT / 64; ++c64) tmem_st64_bias(taddr + (uint32_t)(b * kBN + c64 * 64));
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[b]);
-        }
+        for (int b = 0; b < kTBufs; ++b) tmem_st64_bias(taddr + (uint32_t)(b * kBN));
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+            for (int b = 0; b < kTBufs; ++b) mbar_arrive(&tempty[b]);
         const float bias = 12582912.0f;
         const unsigned long long bias2 =
             ((unsigned long long)__float_as_uint(bias) << 32) | (unsigned long long)__float_as_uint(bias);
         unsigned long long run[kCPT / 2];
 #pragma unroll
         for (int j = 0; j < kCPT / 2; ++j) run[j] = 0ull;  // two fp32 zeros
-        // Software-pipelined over the groups in slices of kSW columns: the TMEM read of the next
-        // slice is in flight while the current one runs through the chains.
-        auto chains = [&](const int (&v)[kSW], int grp, int sl) {
-            const int c = grp / gpc, gi = grp % gpc, ss = c % kSStages;
-            const ulonglong2* sc =
-                reinterpret_cast<const ulonglong2*>(sscale + ss * (kSSlot / 4) + gi * kBN + sl * kSW);
-#pragma unroll
-            for (int j4 = 0; j4 < kSW / 4; ++j4) {
-                const ulonglong2 sv = sc[j4];
-                chain2(run[sl * (kSW / 2) + 2 * j4], v[4 * j4], v[4 * j4 + 1], sv.x, bias2);
-                chain2(run[sl * (kSW / 2) + 2 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3], sv.y, bias2);
-            }
-        };
-        // slice t = kSL * group + sl; before issuing the first slice of a group, wait until the
-        // group's buffer is full (and, for the first group of a chunk, its scales staged)
-        auto issue = [&](int t, int (&v)[kSW]) -> bool {
-            const int grp = t / kSL, sl = t % kSL, b = grp % kTBufs;
-            if (sl == 0) {
-                const int c = grp / gpc;
-                if (grp % gpc == 0 && !wait_or_abort(&sfull[c % kSStages], (c / kSStages) & 1, abort)) return false;
-                if (!wait_or_abort(&tfull[b], (grp / kTBufs) & 1, abort)) return false;
-                tc_fence_after();
-            }
-            tmem_ld8_issue(taddr + (uint32_t)(b * kBN + sl * kSW), v);
-            return true;
-        };
-        // after the last slice of a group: re-arm its buffer, hand it back, free the scale slot
-        auto retire = [&](int grp) {
-            const int b = grp % kTBufs;
-            if (grp + kTBufs < ngroups) {
-#pragma unroll
-                for (int c64 = 0; c64 < kCPT / 64; ++c64) tmem_st64_bias(taddr + (uint32_t)(b * kBN + c64 * 64));
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[b]);
-            if (grp % gpc == gpc - 1) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sempty[(grp / gpc) % kSStages]);
-            }
-        };
-        const int T = ngroups * kSL;
-        int x[kSW], y[kSW];
-        bool ok = issue(0, x);
+        bool ok = true;
+#pragma unroll 1
         for (int grp = 0; grp < ngroups && ok; ++grp) {
-            const int t0 = grp * kSL;
+            const int b = grp % kTBufs, c = grp / gpc, gi = grp % gpc, ss = c % kSStages;
+            if (gi == 0) ok = wait_or_abort(&sfull[ss], (c / kSStages) & 1, abort);
+            if (ok) ok = wait_or_abort(&tfull[b], (grp / kTBufs) & 1, abort);
+            if (!ok) break;
+            tc_fence_after();
+            const ulonglong2* sc = reinterpret_cast<const ulonglong2*>(sscale + ss * (kSSlot / 4) + gi * kBN + h * kCPT);
 #pragma unroll
-            for (int sp = 0; sp < kSL; sp += 2) {
-                tmem_wait_ld(x);
-                ok = issue(t0 + sp + 1, y);
-                chains(x, grp, sp);
-                if (!ok) break;
-                tmem_wait_ld(y);
-                if (sp + 2 == kSL) retire(grp);
-                if (t0 + sp + 2 < T) ok = issue(t0 + sp + 2, x);
-                chains(y, grp, sp + 1);
-                if (!ok) break;
+            for (int half = 0; half < 2; ++half) {
+                int v[32];
+                tmem_ld32(taddr + (uint32_t)(b * kBN + half * 32), v);
+                if (half == 0 && grp > 0) {  // the previous group's buffer: bias stored, hand it back
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[(grp - 1) % kTBufs]);
+                }
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const ulonglong2 sv = sc[half * 8 + j4];
+                    chain2(run[half * 16 + 2 * j4], v[4 * j4], v[4 * j4 + 1], sv.x, bias2);
+                    chain2(run[half * 16 + 2 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3], sv.y, bias2);
+                }
+            }
+            // re-arm this buffer for group grp + kTBufs; the store completes while the next group
+            // is read, and the buffer is handed back after that (the previous group's below)
+            if (grp + kTBufs < ngroups) tmem_st64_bias(taddr + (uint32_t)(b * kBN));
+            if (gi == gpc - 1) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sempty[ss]);
             }
         }
         const int m = m0 + q * 32 + lane;
@@ -407,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         if (ok && !*abort && m < a.M) {
             const float asm_ = a.as[m];
-            const int nb = n0;
+            const int nb = n0 + h * kCPT;
             if constexpr (EPI == kEpiGluSilu || EPI == kEpiGluGelu) {
                 int4* o4 = reinterpret_cast<int4*>(a.out + (size_t)m * (a.N / 2) + nb / 2);
 #pragma unroll
@@ -517,10 +472,14 @@ int launch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& t, in
 }
 }  // namespace
 
-bool gemm_tc_ok(int M, int K, int N, int G, int int4) {
+// Shapes the kernel takes, and only when they fill the GPU with at least one wave of 128 x 128
+// tiles: below that the mma.sync GEMM, with four times as many (smaller) tiles, is faster
+// (measured on B200: M = 256, K = 1024, N = 3072 runs 27 us here against 21 us there).
+bool gemm_tc_ok(int M, int K, int N, int G, int int4, bool any_size) {
     (void)int4;
+    const long long tiles = (long long)((M + kBM - 1) / kBM) * (N / kBN);
     return M >= 1 && N % kBN == 0 && K % kKC == 0 && (G == 32 || G == 64 || G == 128) && K % G == 0 &&
-           encode_fn() != nullptr;
+           (any_size || tiles >= kNumSMs) && encode_fn() != nullptr;
 }
 
 int launch_gemm_tc(const int8_t* aq, const float* as, const void* w, const __half* ws, __half* out,

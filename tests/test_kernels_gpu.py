@@ -60,12 +60,15 @@ def _weights(rng, N, K, G, int4=False):
 @pytest.mark.parametrize("M,K,N,G", [(1, 1024, 3072, 32), (1, 1024, 3072, 128), (2, 2048, 1000, 64),
                                       (5, 640, 520, 32), (8, 1024, 4096, 128), (13, 3072, 1024, 32),
                                       (1, 8192, 264, 32),
-                                      # 16 <= M: the tcgen05 GEMM (INT8, K % 128 == 0, N % 128 == 0,
-                                      # G in 32/64/128) or the mma.sync GEMM (the rest)
+                                      # 16 <= M: the mma.sync GEMM, or the tcgen05 GEMM for shapes of
+                                      # one wave of its tiles or more (both forced below)
                                       (16, 1024, 3072, 32), (127, 2048, 1024, 32), (64, 3072, 1024, 128),
                                       (33, 640, 512, 32), (200, 1024, 4096, 64), (17, 576, 960, 32),
                                       (130, 1024, 96, 128), (64, 128, 32, 32), (128, 256, 64, 64),
-                                      (300, 896, 4864, 32), (513, 1024, 160, 32), (96, 640, 512, 32)])
+                                      (300, 896, 4864, 32), (513, 1024, 160, 32), (96, 640, 512, 32),
+                                      # at least one wave (148) of 128 x 128 tiles: the tcgen05 GEMM
+                                      (128, 256, 18944, 32), (300, 640, 6400, 64), (1100, 1024, 2176, 128),
+                                      (2048, 1024, 1536, 32)])
 def test_matmul_prequantized_bit_exact(L, ref, int4, M, K, N, G):
     if int4 and G % 32:
         pytest.skip("INT4 groups are multiples of 32")
@@ -172,6 +175,17 @@ def test_attention_f16_parity(L, ref, B, S, Skv, Hq, Hkv, D, off, win):
     assert rel_err(got, exp) <= TOL
     # block partition, quadratic exp, lane orders and online-softmax sequence are reproduced
     assert same_bits(got, exp)
+
+
+def test_matmul_tcgen05_every_supported_shape_bit_exact():
+    """The tcgen05 GEMM forced onto every shape it supports (CACTUS_B200_GEMM=tc: K % 128 == 0,
+    N % 128 == 0, G in 32 / 64 / 128, INT8 and INT4, any M), on the GEMM parity cases above,
+    run in a child pytest process."""
+    env = dict(os.environ, CACTUS_B200_GEMM="tc")
+    r = subprocess.run([sys.executable, "-m", "pytest", os.path.abspath(__file__), "-q", "-m", "gpu", "-p",
+                        "no:cacheprovider", "-k", "matmul_prequantized or config1"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
 
 def test_matmul_mma_sync_path_bit_exact():
