@@ -9,14 +9,15 @@
 // one of four TMEM buffers, and the epilogue warps read the groups back in order and continue
 // the fp32 chains in registers while the tensor core fills the next buffers.
 //
-// CTA = 128 activation rows x 128 weight rows, 10 warps:
+// CTA = 128 activation rows x 128 weight rows, 19 warps:
 //   warp 0  producer: 2-D TMA tile loads (cp.async.bulk.tensor, 128-byte swizzle, no
-//           multicast) of the A and B K-chunks (128 bytes of K) into a 4-stage ring, and the
-//           chunk's fp16 group scales into a scale ring;
+//           multicast) of the A and B K-chunks (128 bytes of K) into a 4-stage ring;
 //   warp 1  allocates TMEM (512 columns) and one thread issues the MMAs; tcgen05.commit
 //           signals TMEM buffers full and ring stages free;
-//   warps 2-9  epilogue: warp w reads TMEM lanes 32 * (w % 4) (its tile rows) and columns
-//           64 * ((w - 2) / 4) of each group buffer (tcgen05.ld), continues 64 fp32 chains
+//   warp 18 loads the chunks' fp16 group scales (several chunks per batch of loads) into a
+//           scale ring as fp32;
+//   warps 2-17 epilogue: warp w reads TMEM lanes 32 * (w % 4) (its tile rows) and columns
+//           32 * ((w - 2) / 4) of each group buffer (tcgen05.ld), continues 32 fp32 chains
 //           per thread, then scales by As and writes fp16 (store / residual / GLU).
 // INT4 weights ([N, K/2] nibbles, low = even k): the producer loads the packed chunk with a
 // 2-D TMA tile and, one chunk behind its loads, unpacks it into the swizzled int8 layout
@@ -36,7 +37,9 @@ namespace cb {
 
 namespace {
 constexpr int kBM = 128, kBN = 128, kKC = 128;  // tile rows (A), tile columns (B rows), K bytes per chunk
-constexpr int kStages = 4;
+// ring depth: INT8 stages are 32 KB, INT4 stages 40 KB (with the packed chunk)
+template <int I4>
+constexpr int stages() { return I4 ? 4 : 6; }
 constexpr int kTileA = kBM * kKC, kTileB = kBN * kKC;  // 16 KB each
 constexpr int kPackB = kBN * kKC / 2;                  // INT4: the packed chunk, 8 KB
 // a stage: A tile | B tile (int8, swizzled) | INT4 only: the packed B chunk
@@ -46,12 +49,13 @@ constexpr int kSStages = 8;                             // scale ring (one slot 
 constexpr int kSSlot = 4 * kBN * 4;                     // up to 4 groups x 128 columns, fp32
 constexpr int kTBufs = 4;                               // TMEM group buffers of 128 columns
 constexpr int kTmemCols = kTBufs * kBN;                 // 512
-// 10 warps: eight epilogue warps, two per TMEM lane quarter, each owning 64 columns. (Ten
-// warps leave at most 168 registers a thread, since each SM sub-partition's 16K registers
-// must hold three of them; the epilogue stays below that.)
-constexpr int kWarps = 10, kThreads = kWarps * 32;
-constexpr int kEpiWarps = 8;
-constexpr int kCPT = kBN / 2;      // columns per epilogue thread
+// 18 warps: sixteen epilogue warps, four per TMEM lane quarter, each owning 32 columns. The
+// epilogue is latency-bound (dependent TMEM reads and fp32 chains), so it takes as many warps
+// as the register file holds: each SM sub-partition's 16K registers hold five warps at the
+// 96 registers a thread the 32-column epilogue needs.
+constexpr int kWarps = 19, kThreads = kWarps * 32;  // + producer, MMA issuer, scale loader
+constexpr int kEpiWarps = 16;
+constexpr int kCPT = kBN / 4;      // columns per epilogue thread
 constexpr uint32_t kSpin = 1u << 24;
 
 struct TcArgs {
@@ -115,6 +119,14 @@ __device__ __forceinline__ void tmem_st64_bias(uint32_t taddr) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
         "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+        "r"(b)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st32_bias(uint32_t taddr) {
+    const int b = 0x4B400000;
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
         "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
         "r"(b)
         : "memory");
@@ -190,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int kStage = stage_bytes<I4>();
+    constexpr int kStages = stages<I4>();
     float* const sscale = reinterpret_cast<float*>(smem + kStages * kStage);
     __shared__ uint64_t full[kStages], empty[kStages], cfull[kStages], sfull[kSStages], sempty[kSStages],
         tfull[kTBufs], tempty[kTBufs], drain;
@@ -246,9 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             return true;
         };
         for (int c = 0; c < nchunks; ++c) {
-            const int s = c % kStages, ss = c % kSStages;
+            const int s = c % kStages;
             if (c >= kStages && !wait_or_abort(&empty[s], ((c / kStages) - 1) & 1, abort)) break;
-            if (c >= kSStages && !wait_or_abort(&sempty[ss], ((c / kSStages) - 1) & 1, abort)) break;
             if (lane == 0) {
                 uint8_t* st = smem + s * kStage;
                 if (I4) {
@@ -262,12 +274,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             ++issued;
-            float* sl = sscale + ss * (kSSlot / 4);
-            for (int r = lane; r < kBN; r += 32) {
-                const __half* src = a.ws + (size_t)(n0 + r) * ngroups + c * gpc;
-                for (int g = 0; g < gpc; ++g) sl[g * kBN + r] = h2f(src[g]);
-            }
-            mbar_arrive(&sfull[ss]);
             if (I4 && c >= 1 && !convert(c - 1)) break;
         }
         if (I4 && !*abort && issued == nchunks) convert(nchunks - 1);
@@ -304,12 +310,60 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait_bounded(&drain, 0);
         }
         __syncwarp();
+    } else if (warp == kWarps - 1) {
+        // ---------------------------------------------------------------- group scales
+        // fp16 scales of the tile's rows (lane + 32 i) for kSB chunks at a time: all loads in
+        // flight together (4 / 2 / 1 consecutive scales per row and chunk for G = 32 / 64 / 128,
+        // one aligned 8 / 4 / 2-byte load; rows are ngroups * 2 bytes apart, a multiple of 8
+        // since K % 128 == 0, and the launcher checks the base), then converted to fp32 into
+        // the scale ring as [group][column]
+        constexpr int kSB = kSStages / 2;
+        bool ok = true;
+        for (int c0 = 0; c0 < nchunks && ok; c0 += kSB) {
+            uint2 sreg[kSB][4];
+#pragma unroll
+            for (int j = 0; j < kSB; ++j) {
+                if (c0 + j < nchunks) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const __half* src = a.ws + (size_t)(n0 + lane + 32 * i) * ngroups + (c0 + j) * gpc;
+                        if (gpc == 4) sreg[j][i] = __ldg(reinterpret_cast<const uint2*>(src));
+                        else if (gpc == 2) sreg[j][i].x = __ldg(reinterpret_cast<const unsigned*>(src));
+                        else sreg[j][i].x = __ldg(reinterpret_cast<const unsigned short*>(src));
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kSB; ++j) {
+                const int c = c0 + j, ss = c % kSStages;
+                if (c >= nchunks) break;
+                if (c >= kSStages && !wait_or_abort(&sempty[ss], ((c / kSStages) - 1) & 1, abort)) {
+                    ok = false;
+                    break;
+                }
+                float* sl = sscale + ss * (kSSlot / 4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const __half2 lo = *reinterpret_cast<const __half2*>(&sreg[j][i].x);
+                    const __half2 hi = *reinterpret_cast<const __half2*>(&sreg[j][i].y);
+                    float* d = sl + lane + 32 * i;
+                    d[0] = __low2float(lo);
+                    if (gpc > 1) d[kBN] = __high2float(lo);
+                    if (gpc > 2) {
+                        d[2 * kBN] = __low2float(hi);
+                        d[3 * kBN] = __high2float(hi);
+                    }
+                }
+                mbar_arrive(&sfull[ss]);
+            }
+        }
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int q = warp & 3, h = (warp - 2) >> 2;  // TMEM lane quarter (warp id % 4), column half
+        const int q = warp & 3, h = (warp - 2) >> 2;  // TMEM lane quarter (warp id % 4), column block
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * kCPT);
         // arm every group buffer with the bias (completion 0 of tempty)
-        for (int b = 0; b < kTBufs; ++b) tmem_st64_bias(taddr + (uint32_t)(b * kBN));
+        for (int b = 0; b < kTBufs; ++b)
+            for (int c32 = 0; c32 < kCPT / 32; ++c32) tmem_st32_bias(taddr + (uint32_t)(b * kBN + c32 * 32));
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -331,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const ulonglong2* sc = reinterpret_cast<const ulonglong2*>(sscale + ss * (kSSlot / 4) + gi * kBN + h * kCPT);
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
+            for (int half = 0; half < kCPT / 32; ++half) {
                 int v[32];
                 tmem_ld32(taddr + (uint32_t)(b * kBN + half * 32), v);
                 if (half == 0 && grp > 0) {  // the previous group's buffer: bias stored, hand it back
@@ -349,7 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // re-arm this buffer for group grp + kTBufs; the store completes while the next group
             // is read, and the buffer is handed back after that (the previous group's below)
-            if (grp + kTBufs < ngroups) tmem_st64_bias(taddr + (uint32_t)(b * kBN));
+            if (grp + kTBufs < ngroups) {
+#pragma unroll
+                for (int c32 = 0; c32 < kCPT / 32; ++c32) tmem_st32_bias(taddr + (uint32_t)(b * kBN + c32 * 32));
+            }
             if (gi == gpc - 1) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sempty[ss]);
@@ -443,7 +500,7 @@ bool make_map(CUtensorMap* m, const void* base, int rows, int kbytes, int box_in
 }
 
 template <int I4>
-constexpr size_t smem_bytes() { return (size_t)kStages * stage_bytes<I4>() + (size_t)kSStages * kSSlot + 1024; }
+constexpr size_t smem_bytes() { return (size_t)stages<I4>() * stage_bytes<I4>() + (size_t)kSStages * kSSlot + 1024; }
 
 template <int EPI, int I4>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& t, cudaStream_t st) {
@@ -487,6 +544,7 @@ int launch_gemm_tc(const int8_t* aq, const float* as, const void* w, const __hal
     unsigned* err = dev_error_ptr();
     if (!err) return -1;
     CUtensorMap ma, mb;
+    if (reinterpret_cast<uintptr_t>(ws) & (uintptr_t)(kKC / G * 2 - 1)) return -2;  // scale loads need alignment
     if (!make_map(&ma, aq, M, K, kKC, true)) return -2;  // not TMA-able: the caller falls back
     if (!(int4 ? make_map(&mb, w, N, K / 2, kKC / 2, false) : make_map(&mb, w, N, K, kKC, true))) return -2;
     TcArgs t = {as, nullptr, ws, out, resid, err, M, K, N, G};
