@@ -223,6 +223,11 @@ __device__ __forceinline__ void tma_load_1d_hint(void* smem_dst, const void* gme
         "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// orders this thread's generic-proxy shared-memory accesses before later async-proxy ones
+// (a bulk copy into a buffer that was just read with ordinary loads)
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ void prefetch_l2_bulk(const void* gmem_src, unsigned bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes) : "memory");
 }

@@ -5,6 +5,7 @@
 #include <string>
 
 #include "gemv.cuh"
+#include "gemv_lanes.cuh"
 #include "ops.h"
 
 namespace cb {
@@ -12,17 +13,22 @@ namespace cb {
 namespace {
 
 using KernelFn = void (*)(GemvArgs);
+using KernelLanesFn = void (*)(GemvArgs, int, int);
 
-// CACTUS_B200_GEMV=rows selects the row-streaming kernel where its group-size condition holds.
-// The TMA tile kernel stays the default: on B200 both reach the same rate on a 165 MB weight
-// matrix and the tile kernel is faster on the few-MB projections of a decode step.
-bool gemv_rows_enabled() {
-    static const bool on = [] {
+// GEMV kernel choice, read once per process: the lane-per-row kernel (gemv_lanes.cuh) takes
+// the shapes it supports; CACTUS_B200_GEMV=tile keeps the TMA tile kernel (gemv.cuh) for every
+// shape, CACTUS_B200_GEMV=rows selects the row-streaming kernel where its group-size condition
+// holds.
+int gemv_mode() {
+    static const int mode = [] {
         const char* e = std::getenv("CACTUS_B200_GEMV");
-        return e && std::string(e) == "rows";
+        if (e && std::string(e) == "rows") return 2;
+        if (e && std::string(e) == "tile") return 0;
+        return 1;
     }();
-    return on;
+    return mode;
 }
+bool gemv_rows_enabled() { return gemv_mode() == 2; }
 
 template <int WF, int MT, int RPW, int PRO, int EPI>
 KernelFn fn() {
@@ -90,7 +96,29 @@ KernelFn pick_rows(int mt, int ci) {
     }
 }
 
+template <int WF, int MT>
+KernelLanesFn pick_lanes_combo(int ci) {
+    switch (ci) {
+        case 0: return &qgemv_lanes_kernel<WF, MT, kProPreq, kEpiStore>;
+        case 1: return &qgemv_lanes_kernel<WF, MT, kProQuant, kEpiStore>;
+        case 2: return &qgemv_lanes_kernel<WF, MT, kProQuant, kEpiResidual>;
+        case 3: return &qgemv_lanes_kernel<WF, MT, kProRmsNormQuant, kEpiStore>;
+        case 4: return &qgemv_lanes_kernel<WF, MT, kProRmsNormQuant, kEpiGluSilu>;
+        case 5: return &qgemv_lanes_kernel<WF, MT, kProRmsNormQuant, kEpiGluGelu>;
+    }
+    return nullptr;
+}
+template <int WF>
+KernelLanesFn pick_lanes(int mt, int ci) {
+    switch (mt) {
+        case 1: return pick_lanes_combo<WF, 1>(ci);
+        case 2: return pick_lanes_combo<WF, 2>(ci);
+        default: return pick_lanes_combo<WF, 4>(ci);
+    }
+}
+
 std::mutex g_attr_mu;
+bool g_lanes_attr[2][5][kNumCombos] = {};
 bool g_attr_set[2][9][5][kNumCombos] = {};
 // row-streaming variants: shared-memory attribute set, resident blocks per SM (0: unknown)
 bool g_rows_attr[2][9][kNumCombos] = {};
@@ -138,6 +166,15 @@ void gemv_prepare() {
                                  cudaSuccess)
                         done = true;
                 }
+    for (int wf = 0; wf < 2; ++wf)
+        for (int mt : {1, 2, 4})
+            for (int ci = 0; ci < kNumCombos; ++ci) {
+                bool& done = g_lanes_attr[wf][mt][ci];
+                if (done) continue;
+                KernelLanesFn f = wf ? pick_lanes<1>(mt, ci) : pick_lanes<0>(mt, ci);
+                if (f && cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) == cudaSuccess)
+                    done = true;
+            }
     for (int wf = 0; wf < 2; ++wf)
         for (int mt : {1, 2, 4, 8})
             for (int ci = 0; ci < kNumCombos; ++ci) {
@@ -193,6 +230,44 @@ static int launch_gemv_rows(const GemvCall& c, int mt, int ci, const GemvArgs& a
     return cudaLaunchKernelEx(&cfg, f, a) == cudaSuccess ? 0 : -1;
 }
 
+// Lane-per-row launch (gemv_lanes.cuh); -2 when the shape does not qualify. One block per SM
+// (its rings take most of the shared memory), warps with row blocks only, and as many ring
+// slots per warp as fit (2 to 8).
+static int launch_gemv_lanes(const GemvCall& c, int mt, int ci, const GemvArgs& a, cudaStream_t st) {
+    if (mt > 4 || c.K % 128 || !(c.G == 32 || c.G == 64 || c.G == 128)) return -2;
+    const GemvLanesLayout L = gemv_lanes_layout(c.int4, mt, c.K, c.G);
+    const int nrb = (c.N + 31) / 32;
+    const int grid = nrb < kNumSMs ? nrb : kNumSMs;
+    int wpc = (nrb + grid - 1) / grid;
+    if (wpc > kGemvWarps) wpc = kGemvWarps;
+    int S = (kSmemLimit - L.fixed) / (wpc * L.slot);
+    if (S > kLaneMaxSlots) S = kLaneMaxSlots;
+    if (S < 2) return -2;
+    const size_t smem = (size_t)L.fixed + (size_t)wpc * S * L.slot;
+    KernelLanesFn f = c.int4 ? pick_lanes<1>(mt, ci) : pick_lanes<0>(mt, ci);
+    if (!f) return -2;
+    {
+        std::lock_guard<std::mutex> lk(g_attr_mu);
+        bool& done = g_lanes_attr[c.int4][mt][ci];
+        if (!done) {
+            if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) != cudaSuccess)
+                return -1;
+            done = true;
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (c.pdl || pdl_flag()) ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, f, a, S, wpc) == cudaSuccess ? 0 : -1;
+}
+
 int launch_gemv(const GemvCall& c, cudaStream_t st) {
     const int mt = mt_of(c.M);
     // rows per tile: 8 for narrow outputs (>= 128 tiles at N = 1024), 16 for mid-size, 32 for
@@ -241,6 +316,10 @@ int launch_gemv(const GemvCall& c, cudaStream_t st) {
     a.S = S;
     if (gemv_rows_enabled()) {
         const int r = launch_gemv_rows(c, mt, ci, a, st);
+        if (r != -2) return r;
+    }
+    if (gemv_mode() == 1) {
+        const int r = launch_gemv_lanes(c, mt, ci, a, st);
         if (r != -2) return r;
     }
     cudaLaunchConfig_t cfg = {};
