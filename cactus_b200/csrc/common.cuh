@@ -223,6 +223,16 @@ __device__ __forceinline__ void tma_load_1d_hint(void* smem_dst, const void* gme
         "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// 2-D tiled TMA load (no multicast) at (x = innermost byte coordinate, y = row), with an L2
+// cache-policy hint; `map` is a __grid_constant__ kernel parameter
+__device__ __forceinline__ void tma_load_2d_tile(void* dst, const void* map, int x, int y, uint64_t* bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
 // orders this thread's generic-proxy shared-memory accesses before later async-proxy ones
 // (a bulk copy into a buffer that was just read with ordinary loads)
 __device__ __forceinline__ void fence_proxy_async_shared() {

@@ -42,6 +42,7 @@ struct GemvArgs {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvRedSq = 64;  // prologue scratch: per-warp maxima below, sums of squares from here
 
 struct GemvLayout {
     int R, wrow, ng, stage_w, stage_s, stage_bytes, S, gpj, pairs;
@@ -171,16 +172,17 @@ __device__ __forceinline__ int8_t quant_act(float v, float inv, bool vec) {
 // Activation prologue of both GEMV kernels: the M rows of x (or the pre-quantised rows) into
 // `act` (int8, [MT][K]; INT4 weights: each 8-element block permuted so that dp4a pairs the even
 // and the odd k with the low and the high nibbles), the per-row scales into `as`, and for INT4
-// the per-group activation sums into `asum`. `xs` holds MT * K halves, `red` 72 floats (the
-// per-warp maxima and the sums of squares). Ends with a block barrier.
-template <int WF, int MT, int PRO>
+// the per-group activation sums into `asum`. `xs` holds MT * K halves, `red` kGemvRedSq + 8
+// floats (the per-warp maxima of the NT / 32 warps (MT * NT / 32 <= kGemvRedSq), then the sums
+// of squares). Ends with a block barrier.
+template <int WF, int MT, int PRO, int NT = kGemvThreads>
 __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, int8_t* act, int* asum, float* as, __half* xs,
                                               float* red) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = a.K, G = a.G, M = a.M;
     const int ng = K / G;
     if constexpr (PRO == (int)Pro::PREQ) {
-        for (int i = tid; i < M * K; i += kGemvThreads) {
+        for (int i = tid; i < M * K; i += NT) {
             const int m = i / K, k = i % K;
             int8_t v = a.aq[i];
             if constexpr (WF == 1) {
@@ -200,15 +202,15 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, int8_t* act, in
         if ((K & 7) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0) {
             const int4* src = reinterpret_cast<const int4*>(a.x);
             int4* dst = reinterpret_cast<int4*>(xs);
-            for (int i = tid; i < M * K / 8; i += kGemvThreads) dst[i] = src[i];
+            for (int i = tid; i < M * K / 8; i += NT) dst[i] = src[i];
         } else {
-            for (int i = tid; i < M * K; i += kGemvThreads) xs[i] = a.x[i];
+            for (int i = tid; i < M * K; i += NT) xs[i] = a.x[i];
         }
         __syncthreads();
         if constexpr (PRO == (int)Pro::RMSNORM_QUANT) {
             if (warp < M) {
                 const float ss = rms_sumsq_warp(xs + warp * K, K);
-                if (lane == 0) red[64 + warp] = ss;
+                if (lane == 0) red[kGemvRedSq + warp] = ss;
             }
             __syncthreads();
         }
@@ -216,12 +218,12 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, int8_t* act, in
             float inv_rms = 0.0f;
             __half inv16 = __float2half_rn(0.0f);
             if constexpr (PRO == (int)Pro::RMSNORM_QUANT) {
-                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(red[64 + m], (float)K), a.eps));
+                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(red[kGemvRedSq + m], (float)K), a.eps));
                 inv_rms = __fdiv_rn(1.0f, rms);
                 inv16 = __float2half_rn(inv_rms);
             }
             float mx = 0.0f;
-            for (int k = tid; k < K; k += kGemvThreads) {
+            for (int k = tid; k < K; k += NT) {
                 __half v = xs[m * K + k];
                 if constexpr (PRO == (int)Pro::RMSNORM_QUANT) {
                     v = (k < vec_end) ? __hmul(__hmul(v, inv16), a.norm_w[k])
@@ -231,18 +233,18 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, int8_t* act, in
                 mx = fmaxf(mx, fabsf(h2f(v)));
             }
             mx = warp_max(mx);
-            if (lane == 0) red[m * 8 + warp] = mx;
+            if (lane == 0) red[m * (NT / 32) + warp] = mx;
         }
         __syncthreads();
         for (int m = 0; m < M; ++m) {
-            float mx = red[m * 8];
+            float mx = red[m * (NT / 32)];
 #pragma unroll
-            for (int w = 1; w < kGemvWarps; ++w) mx = fmaxf(mx, red[m * 8 + w]);
+            for (int w = 1; w < NT / 32; ++w) mx = fmaxf(mx, red[m * (NT / 32) + w]);
             float scale = __fdiv_rn(mx, 127.0f);
             if (scale < 1e-10f) scale = 1e-10f;
             const float inv = __fdiv_rn(1.0f, scale);
             if (tid == 0) as[m] = scale;
-            for (int k = tid; k < K; k += kGemvThreads) {
+            for (int k = tid; k < K; k += NT) {
                 const int8_t q = quant_act(h2f(xs[m * K + k]), inv, k < vec_end);
                 if constexpr (WF == 1) {
                     const int blk = k >> 3, e = k & 7;
@@ -257,7 +259,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, int8_t* act, in
         __syncthreads();
     }
     if constexpr (WF == 1) {  // per-group activation sums for the unsigned-nibble dot product
-        for (int i = tid; i < M * ng; i += kGemvThreads) {
+        for (int i = tid; i < M * ng; i += NT) {
             const int m = i / ng, g = i % ng;
             int s = 0;
             for (int k = 0; k < G; ++k) s += act[m * K + g * G + k];  // permutation stays inside 8-blocks

@@ -6,58 +6,63 @@
 // quantisation, optionally RMSNorm) and epilogues (store, residual, SiLU / GELU GLU).
 //
 // Layout of the work: lane l of a warp owns output row 32 * b + l of the warp's row blocks b
-// and walks that row's K in chunks of 256 (or 128) k, the whole fp32 chain of the row in
-// its own register — so the chain needs no cross-lane step and a chunk costs a lane about
-// one instruction per 2 weight bytes. Each warp feeds itself: for every chunk it issues one
-// 1-D bulk copy per row (cp.async.bulk, no multicast, L2 evict-first) into a slot of its own
-// S-deep ring, rows padded by 16 bytes so the lanes' 16-byte shared loads fall into different
-// banks; one mbarrier per slot. The warp re-issues a slot once it has read it, so no block
-// barrier is needed after the activation prologue. Each lane also prefetches its row's group
-// scales for the next chunk with plain 4- or 2-byte loads.
+// and walks that row's K in chunks of 128 weight bytes, the whole fp32 chain of the row in its
+// own register — so the chain needs no cross-lane step and a chunk costs a lane about one
+// instruction per 2 weight bytes. Each warp feeds itself: a slot of its own S-deep ring holds
+// nb consecutive chunks of its 32 rows, loaded by nb 2-D TMA tile copies (cp.async.bulk.tensor,
+// box of 128 bytes x 32 rows, 128-byte swizzle, no multicast, L2 evict-first) on one mbarrier;
+// the swizzle puts the lanes' 16-byte shared loads of 8 consecutive rows into different banks.
+// The warp re-issues a slot once it has read it, so no block barrier is needed after the
+// activation prologue. Each lane also prefetches its row's group scales for the next chunk
+// with plain 4- or 2-byte loads.
 #pragma once
 #include "gemv.cuh"
 
 namespace cb {
 
-constexpr int kLaneMaxSlots = 8;
+constexpr int kLaneMaxSlots = 16;
+constexpr int kLanesThreads = 384;  // 12 row-owning warps: more independent streams per SM
+constexpr int kLanesWarps = kLanesThreads / 32;
 
 struct GemvLanesLayout {
-    int kc, kcb, rs, slot;  // k per chunk, weight bytes per row chunk, padded row stride, slot bytes
+    int kc, kcb, slot;  // k per chunk, weight bytes per row chunk (128), slot bytes (32 rows)
     int off_act, off_asum, off_as, off_xs, off_red, off_bars, off_warps, fixed;
 };
 
 __host__ __device__ inline GemvLanesLayout gemv_lanes_layout(int wf, int mt, int K, int G) {
     GemvLanesLayout L;
-    L.kc = (K % 256 == 0) ? 256 : 128;
-    L.kcb = wf ? L.kc / 2 : L.kc;
-    L.rs = L.kcb + 16;
-    L.slot = 32 * L.rs;
+    L.kcb = 128;
+    L.kc = wf ? 256 : 128;
+    L.slot = 32 * L.kcb;
+    (void)K;
     int off = 0;
     L.off_act = off;   off += align_up(mt * K, 128);
     L.off_asum = off;  off += align_up(mt * (K / G) * 4, 128);
     L.off_as = off;    off += 128;
     L.off_xs = off;    off += align_up(mt * K * 2, 128);
     L.off_red = off;   off += align_up(72 * 4, 128);
-    L.off_bars = off;  off += align_up(kGemvWarps * kLaneMaxSlots * 8, 128);
-    L.off_warps = off;
-    L.fixed = off;
+    L.off_bars = off;  off += align_up(kLanesWarps * kLaneMaxSlots * 8, 128);
+    L.off_warps = align_up(off, 1024);  // swizzled TMA destinations: 1024-byte aligned slots
+    L.fixed = L.off_warps + 1024;       // + slack for the runtime alignment of the window
     return L;
 }
 
-template <int WF, int MT, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1) qgemv_lanes_kernel(GemvArgs a, int S, int wpc) {
+template <int WF, int MT, int GT, int PRO, int EPI>
+__global__ void __launch_bounds__(kLanesThreads, 1)
+    qgemv_lanes_kernel(const __grid_constant__ CUtensorMap wmap, GemvArgs a, int S, int wpc, int nb) {
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvLanesLayout L = gemv_lanes_layout(WF, MT, a.K, a.G);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = a.K, N = a.N, G = a.G, M = a.M;
-    const int ng = K / G, kc = L.kc, kcb = L.kcb, nch = K / kc, gpc = kc / G;
-    const size_t wrow = WF ? (size_t)K / 2 : (size_t)K;
+    constexpr int G = GT;  // the group size is a template parameter: the chunk loops unroll
+    const int K = a.K, N = a.N, M = a.M;
+    constexpr int kc = WF ? 256 : 128, gpc = kc / G;
+    const int ng = K / G, kcb = L.kcb, nch = K / kc;
     int8_t* act = reinterpret_cast<int8_t*>(smem + L.off_act);
     int* asum = reinterpret_cast<int*>(smem + L.off_asum);
     float* as = reinterpret_cast<float*>(smem + L.off_as);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.off_bars) + warp * kLaneMaxSlots;
-    uint8_t* wsm = smem + L.off_warps + (size_t)warp * S * L.slot;
-    const uint8_t* wbase = reinterpret_cast<const uint8_t*>(a.w);
+    uint8_t* const ring0 = smem + L.off_warps;
+    uint8_t* wsm = ring0 + ((1024u - (smem_u32(ring0) & 1023u)) & 1023u) + (size_t)warp * S * nb * L.slot;
     const uint16_t* sbase = reinterpret_cast<const uint16_t*>(a.ws);
     const uint64_t policy = l2_policy_evict_first();
 
@@ -67,26 +72,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_lanes_kernel(GemvArgs a
     const int nrb = (N + 31) / 32;
     const int my_rb = (warp < wpc && first_rb < nrb) ? (nrb - first_rb + nw - 1) / nw : 0;
     const int T = my_rb * nch;  // (row block, chunk) tasks of this warp, in order
+    const int slot = nb * L.slot;  // a ring slot holds nb consecutive chunks (nch % nb == 0)
 
     if (lane == 0)
         for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
     __syncwarp();
-    auto issue = [&](int t) {
-        if (t >= T) return;
-        const int rb = first_rb + (t / nch) * nw, c = t % nch, s = t % S;
-        const int row0 = rb * 32, nval = min(32, N - row0);
-        if (lane == 0) mbar_arrive_expect_tx(&bars[s], (unsigned)(nval * kcb));
-        __syncwarp();
-        if (lane < nval)
-            tma_load_1d_hint(wsm + (size_t)s * L.slot + lane * L.rs, wbase + (size_t)(row0 + lane) * wrow + (size_t)c * kcb,
-                             (unsigned)kcb, &bars[s], policy);
+    // slot task v: chunks v * nb .. v * nb + nb - 1 (one row block) into slot v % S
+    auto issue = [&](int v) {
+        if (v * nb >= T) return;
+        const int u = v * nb, rb = first_rb + (u / nch) * nw, c = u % nch, s = v % S;
+        if (lane == 0) {  // rows past N read as zeros and still count in the transaction
+            mbar_arrive_expect_tx(&bars[s], (unsigned)slot);
+            for (int b = 0; b < nb; ++b)
+                tma_load_2d_tile(wsm + (size_t)s * slot + b * L.slot, &wmap, (c + b) * kcb, rb * 32, &bars[s],
+                                 policy);
+        }
     };
     // weights do not depend on the previous kernel: the first chunks stream while it finishes
-    for (int t = 0; t < S; ++t) issue(t);
+    for (int v = 0; v < S; ++v) issue(v);
     pdl_launch_dependents();
     pdl_wait();
-    gemv_prologue<WF, MT, PRO>(a, act, asum, as, reinterpret_cast<__half*>(smem + L.off_xs),
+    gemv_prologue<WF, MT, PRO, kLanesThreads>(a, act, asum, as, reinterpret_cast<__half*>(smem + L.off_xs),
                                reinterpret_cast<float*>(smem + L.off_red));
 
     // the lane's row scales of chunk t: gpc consecutive fp16 values (4-byte loads when gpc is
@@ -112,30 +119,35 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_lanes_kernel(GemvArgs a
     bool ok = true;
     int t = 0;
     for (; t < T; ++t) {
-        const int s = t % S, c = t % nch;
+        const int v = t / nb, b = t - v * nb, s = v % S, c = t % nch;
         const int row = (first_rb + (t / nch) * nw) * 32 + lane;
         load_scales(t + 1, scn);
-        if (!mbar_wait_bounded(&bars[s], (unsigned)((t / S) & 1))) {
+        if (b == 0 && !mbar_wait_bounded(&bars[s], (unsigned)((v / S) & 1))) {
             ok = false;
             break;
         }
-        const uint8_t* wr = wsm + (size_t)s * L.slot + lane * L.rs;
-        for (int gi = 0; gi < gpc; ++gi) {
-            int acc[MT];
+        // row `lane` of the chunk: 16-byte piece j at (j ^ (lane & 7)) * 16 (128-byte swizzle)
+        const uint8_t* wr = wsm + (size_t)s * slot + b * L.slot + lane * 128;
+        const int sw = lane & 7;
 #pragma unroll
-            for (int m = 0; m < MT; ++m) acc[m] = 0;
+        for (int gi = 0; gi < gpc; ++gi) {
+            // integer group sums are exact in any order: two independent dp4a chains per row
+            int acc[MT][2];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[m][0] = acc[m][1] = 0;
             const int kb = c * kc + gi * G;  // first k of the group
             if constexpr (WF == 0) {
+#pragma unroll
                 for (int q = 0; q < G / 16; ++q) {
-                    const int4 wv = *reinterpret_cast<const int4*>(wr + gi * G + q * 16);
+                    const int4 wv = *reinterpret_cast<const int4*>(wr + ((((gi * G) >> 4) + q) ^ sw) * 16);
 #pragma unroll
                     for (int m = 0; m < MT; ++m) {
                         if (m < M) {
                             const int4 av = *reinterpret_cast<const int4*>(act + m * K + kb + q * 16);
-                            acc[m] = dp4a_ss(av.x, wv.x, acc[m]);
-                            acc[m] = dp4a_ss(av.y, wv.y, acc[m]);
-                            acc[m] = dp4a_ss(av.z, wv.z, acc[m]);
-                            acc[m] = dp4a_ss(av.w, wv.w, acc[m]);
+                            acc[m][q & 1] = dp4a_ss(av.x, wv.x, acc[m][q & 1]);
+                            acc[m][q & 1] = dp4a_ss(av.y, wv.y, acc[m][q & 1]);
+                            acc[m][q & 1] = dp4a_ss(av.z, wv.z, acc[m][q & 1]);
+                            acc[m][q & 1] = dp4a_ss(av.w, wv.w, acc[m][q & 1]);
                         }
                     }
                 }
@@ -143,8 +155,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_lanes_kernel(GemvArgs a
                 // 16 packed bytes = 32 k; activations permuted inside 8-blocks by the prologue so
                 // that even k pair with low nibbles and odd k with high nibbles (nibble ^ 8 is
                 // the value + 8, corrected with 8 * the group's activation sum)
+#pragma unroll
                 for (int q = 0; q < G / 32; ++q) {
-                    const int4 wv = *reinterpret_cast<const int4*>(wr + gi * (G / 2) + q * 16);
+                    const int4 wv = *reinterpret_cast<const int4*>(wr + ((((gi * (G / 2)) >> 4) + q) ^ sw) * 16);
                     const unsigned ww[4] = {(unsigned)wv.x, (unsigned)wv.y, (unsigned)wv.z, (unsigned)wv.w};
 #pragma unroll
                     for (int m = 0; m < MT; ++m) {
@@ -157,28 +170,30 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_lanes_kernel(GemvArgs a
                             for (int e = 0; e < 4; ++e) {
                                 const unsigned lo = (ww[e] & 0x0F0F0F0Fu) ^ 0x08080808u;
                                 const unsigned hi = ((ww[e] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
-                                acc[m] = dp4a_su(ae[e], lo, acc[m]);
-                                acc[m] = dp4a_su(ao[e], hi, acc[m]);
+                                acc[m][0] = dp4a_su(ae[e], lo, acc[m][0]);
+                                acc[m][1] = dp4a_su(ao[e], hi, acc[m][1]);
                             }
                         }
                     }
                 }
 #pragma unroll
                 for (int m = 0; m < MT; ++m)
-                    if (m < M) acc[m] -= 8 * asum[m * ng + c * gpc + gi];
+                    if (m < M) acc[m][0] -= 8 * asum[m * ng + c * gpc + gi];
             }
             const int wi = (gi >> 1) & 3;  // register selects, not an indexed (local-memory) array
-            const uint32_t sw = wi == 0 ? sc[0] : wi == 1 ? sc[1] : wi == 2 ? sc[2] : sc[3];
-            const float scale = h2f_bits((uint16_t)(gpc >= 2 ? ((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu)) : sw));
+            const uint32_t swd = wi == 0 ? sc[0] : wi == 1 ? sc[1] : wi == 2 ? sc[2] : sc[3];
+            const float scale = h2f_bits((uint16_t)(gpc >= 2 ? ((gi & 1) ? (swd >> 16) : (swd & 0xFFFFu)) : swd));
 #pragma unroll
             for (int m = 0; m < MT; ++m)
-                if (m < M) run[m] = fmaf(i2f_small(acc[m]), scale, run[m]);
+                if (m < M) run[m] = fmaf(i2f_small(acc[m][0] + acc[m][1]), scale, run[m]);
         }
-        // the slot is read: hand it to the chunk S ahead (after the generic-proxy reads, before
-        // the bulk copy writes it)
-        __syncwarp();
-        fence_proxy_async_shared();
-        issue(t + S);
+        // the slot is read: hand it to the slot task S ahead (after the generic-proxy reads,
+        // before the bulk copy writes it)
+        if (b == nb - 1) {
+            __syncwarp();
+            fence_proxy_async_shared();
+            issue(v + S);
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) sc[i] = scn[i];
         if (c == nch - 1) {  // row complete: C[m, row]
@@ -207,7 +222,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_lanes_kernel(GemvArgs a
     if (!ok) {
         if (lane == 0) report_dev_error(kDevTmaTimeout);
         // no copy may land after the block leaves: wait (bounded) for the ones issued
-        for (int u = t; u < t + S && u < T; ++u) mbar_wait_bounded(&bars[u % S], (unsigned)((u / S) & 1));
+        for (int v = t / nb; v < t / nb + S && v * nb < T; ++v) mbar_wait_bounded(&bars[v % S], (unsigned)((v / S) & 1));
     }
 }
 

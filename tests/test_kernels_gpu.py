@@ -60,6 +60,9 @@ def _weights(rng, N, K, G, int4=False):
 @pytest.mark.parametrize("M,K,N,G", [(1, 1024, 3072, 32), (1, 1024, 3072, 128), (2, 2048, 1000, 64),
                                       (5, 640, 520, 32), (8, 1024, 4096, 128), (13, 3072, 1024, 32),
                                       (1, 8192, 264, 32),
+                                      # wide outputs: the lane-per-row GEMV (ragged N)
+                                      (1, 1024, 19000, 32), (3, 2048, 20480, 128), (4, 512, 18950, 32),
+                                      (2, 1024, 6150, 128), (1, 768, 16390, 32),
                                       # 16 <= M: the mma.sync GEMM, or the tcgen05 GEMM for shapes of
                                       # one wave of its tiles or more (both forced below)
                                       (16, 1024, 3072, 32), (127, 2048, 1024, 32), (64, 3072, 1024, 128),
@@ -208,6 +211,20 @@ def test_gemv_row_streaming_path_bit_exact():
                         "no:cacheprovider", "-k", "matmul_prequantized or config1 or llama_down"],
                        env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_gemv_lane_path_bit_exact():
+    """The lane-per-row GEMV (the default for wide outputs; forced for every shape it
+    supports with CACTUS_B200_GEMV=lanes, read once per process) on every GEMV parity case above
+    and on the engine's decode paths (fused RMSNorm prologues, GLU epilogues), in child pytest
+    processes."""
+    env = dict(os.environ, CACTUS_B200_GEMV="lanes")
+    here = os.path.dirname(os.path.abspath(__file__))
+    for path, sel in ((os.path.abspath(__file__), "matmul_prequantized or config1 or llama_down or linear"),
+                      (os.path.join(here, "test_engine_gpu.py"), "not qwen3_0_6b")):
+        r = subprocess.run([sys.executable, "-m", "pytest", path, "-q", "-m", "gpu", "-p", "no:cacheprovider",
+                            "-k", sel], env=env, capture_output=True, text=True, timeout=900)
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
 
 # L_ >= 512: the key-split kernels (attention_split.cu); below: one CTA per query
