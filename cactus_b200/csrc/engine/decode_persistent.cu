@@ -7,15 +7,20 @@
 //
 // Why: at batch 1 each projection is a few MB, so a kernel per op is bound by launch and
 // dependency latency, not by HBM. Here one block per SM stays resident for the token:
-//  * warp 15 of every block is a producer that streams the block's share of every weight
+//  * warp 11 of every block is a producer that streams the block's share of every weight
 //    matrix of the token (a fixed row range per matrix, 8-row units) through a ring of
 //    shared-memory slots with 1-D TMA bulk copies (no multicast), full/empty mbarriers per
 //    slot. Weights do not depend on activations, so the stream runs ahead of the layer
 //    dependency chain by the ring's depth and HBM stays busy across phase boundaries;
-//  * warps 0-14 consume: per phase they rebuild the quantised activations in shared memory
-//    (every block redundantly, which is cheaper than another grid barrier), reduce their
-//    rows and write outputs; grid-wide barriers (one counter, bounded spins, release/acquire)
-//    separate phases: QKV | attention | O | gate-up | down, five per layer.
+//  * warps 0-10 consume: per phase they rebuild the quantised activations in shared memory
+//    (every block redundantly, which is cheaper than another exchange), reduce their rows and
+//    write outputs. Phases (QKV | attention | O | gate-up | down, five per layer) hand data
+//    over as tagged words (fp16 bits + the writer's version tag, see PArgs): a block polls
+//    the words it needs until they carry the expected version, so there is no grid barrier
+//    and a phase starts as soon as its own inputs exist (the attention blocks wait for their
+//    head's rows only). Reuse of a buffer is ordered by the data flow: every block writes
+//    QKV and gate-up rows (the grid is sized so), and every reader waits for whole vectors,
+//    so a block can only overwrite a version once every block has read it.
 //  * blocks 0..Hq-1 run one attention head each (the reference-order core).
 //  * the lm head keeps a per-block first-max key; the last block to finish combines them,
 //    writes the next token, advances the device state and re-arms the sync words.
@@ -95,6 +100,45 @@ __device__ __forceinline__ void set_abort(const PArgs& a, unsigned code) {
     report_dev_error(code);
 }
 
+// ------------------------------------------------------------------ tagged activation words
+__device__ __forceinline__ unsigned vtag(const PArgs& a, int v) { return 1u + (a.tag_base + (unsigned)v) % 65535u; }
+__device__ __forceinline__ void st_tagged(uint32_t* p, __half h, unsigned tag) {
+    const uint32_t w = (tag << 16) | (uint32_t)__half_as_ushort(h);
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
+}
+__device__ __forceinline__ uint4 ld_relaxed_v4(const uint32_t* p) {
+    uint4 v;
+    asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ bool tagged4(const uint4& v, unsigned tag) {
+    return ((v.x >> 16) == tag) & ((v.y >> 16) == tag) & ((v.z >> 16) == tag) & ((v.w >> 16) == tag);
+}
+__device__ __forceinline__ __half word_h(uint32_t w) { return __ushort_as_half((unsigned short)(w & 0xFFFFu)); }
+
+// Bounded poll of the next attempt: false once `it` passes the spin limit (the abort word and
+// the device error are set) or, checked every 64 attempts, once another block aborted.
+__device__ __forceinline__ bool poll_go_on(const PArgs& a, uint32_t it) {
+    if (it > a.spin_limit) {
+        set_abort(a, kDevFlagTimeout);
+        return false;
+    }
+    return (it & 63) != 63 || !ld_volatile_u32(&a.sync->abort);
+}
+
+// Polls one tagged word until it carries `tag`.
+__device__ __forceinline__ bool poll_word(const PArgs& a, const uint32_t* p, unsigned tag, uint32_t& w) {
+    w = ld_relaxed_gpu(p);
+    for (uint32_t it = 0; (w >> 16) != tag; ++it) {
+        if (!poll_go_on(a, it)) return false;
+        w = ld_relaxed_gpu(p);
+    }
+    return true;
+}
+
 // ------------------------------------------------------------------ producer (one thread)
 __device__ void producer(const PArgs& a, uint8_t* ring, uint64_t* full, uint64_t* empty) {
     const int NS = a.nslots, sb = a.slot_w + a.slot_s;
@@ -140,6 +184,7 @@ struct Cs {  // consumer shared memory
     float* red;   // [64]
     float* as;    // activation scale of the current job
     int* flag;
+    int* fail;    // set (never cleared) by a thread whose poll gave up
     unsigned long long* best;  // [16]
 };
 
@@ -169,6 +214,60 @@ __device__ __forceinline__ void load_vec(const Cs& m, const __half* src, int K, 
         }
     }
     cbar();
+}
+
+constexpr int kMaxR = 4;  // 16-byte chunks of a tagged vector a consumer thread has in flight
+
+// Stages K tagged fp16 activations (K % 4 == 0) into xs (with `transposed`, also the
+// lane-major copy xsT) once every word carries `tag`: each thread issues the loads of up to
+// kMaxR of its 16-byte chunks at once, then re-polls the ones not yet written. False (after
+// the block barrier, in every thread) when a poll gave up.
+__device__ __forceinline__ bool load_tagged(const Cs& m, const PArgs& a, const uint32_t* src, int K, unsigned tag,
+                                            bool transposed) {
+    const int tid = threadIdx.x, n4 = K / 4, TS = lanemajor_stride(K);
+    for (int base = 0; base < n4; base += kPC * kMaxR) {
+        uint4 v[kMaxR];
+        unsigned pend = 0;
+#pragma unroll
+        for (int r = 0; r < kMaxR; ++r) {
+            const int i = base + tid + r * kPC;
+            if (i < n4) {
+                v[r] = ld_relaxed_v4(src + 4 * i);
+                if (!tagged4(v[r], tag)) pend |= 1u << r;
+            }
+        }
+        for (uint32_t it = 0; pend; ++it) {
+            if (!poll_go_on(a, it)) {
+                *m.fail = 1;
+                break;
+            }
+#pragma unroll
+            for (int r = 0; r < kMaxR; ++r) {
+                if (pend & (1u << r)) {
+                    v[r] = ld_relaxed_v4(src + 4 * (base + tid + r * kPC));
+                    if (tagged4(v[r], tag)) pend &= ~(1u << r);
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kMaxR; ++r) {
+            const int i = base + tid + r * kPC;
+            if (i < n4) {
+                *reinterpret_cast<uint2*>(m.xs + 4 * i) =
+                    make_uint2((v[r].x & 0xFFFFu) | (v[r].y << 16), (v[r].z & 0xFFFFu) | (v[r].w << 16));
+                if (transposed) {
+                    const uint32_t w[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int k = 4 * i + j;
+                        m.xsT[(k & 15) * TS + (k >> 4)] = word_h(w[j]);
+                    }
+                }
+            }
+        }
+    }
+    cbar();
+    return *m.fail == 0;
 }
 
 // RMSNorm sum of squares (rms_sumsq_warp's order, K % 16 == 0) from the lane-major copy:
@@ -277,8 +376,11 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
 
 // One projection of the block's rows: grouped INT8 GEMV (exact int32 group sums, fp32 FMA
 // chain over the groups in order, times the activation scale -> fp16) + epilogue.
+// Outputs go to `out` as tagged words (`tag_out`; the residual read polls for `tag_res`),
+// the lm head's logits to `lm_out` as plain fp16.
 __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const Cs& m, uint8_t* ring, uint64_t* full,
-                         uint64_t* empty, unsigned& kslot, __half* out, unsigned long long& best) {
+                                         uint64_t* empty, unsigned& kslot, uint32_t* out, __half* lm_out,
+                                         unsigned tag_out, unsigned tag_res, unsigned long long& best) {
     const int tid = threadIdx.x;
     const JobW jw = job_w(a, j);
     int r0, r1;
@@ -300,15 +402,21 @@ __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const C
         const int s = (int)(kslot % NS);
         const unsigned par = (kslot / NS) & 1;
         const int rows = min(spr, r1 - r);
-        // the residual row of this thread's output, read before the slot wait (the hidden
-        // state is stable since the last grid barrier)
-        const __half res = (epi == kEpiResid && tid < rows) ? __ldcg(out + r + tid) : __float2half_rn(0.0f);
+        // the residual row of this thread's output, read before the slot wait (written by this
+        // block's previous projection into the same rows, or by the embedding)
+        __half res = __float2half_rn(0.0f);
+        if (epi == kEpiResid && tid < rows) {
+            uint32_t w;
+            if (!poll_word(a, out + r + tid, tag_res, w)) *m.fail = 1;
+            res = word_h(w);
+        }
         if (tid == 0) *m.flag = wait_abortable(&full[s], par, &a.sync->abort, 32, a.spin_limit) ? 1 : 0;
         cbar();
         if (!*m.flag) {
             if (tid == 0) set_abort(a, kDevTmaTimeout);
             return false;
         }
+        if (*m.fail) return false;
         mbar_wait_bounded(&full[s], par);  // completed already: makes the copy visible to this thread
         const uint8_t* wsl = ring + (size_t)s * sb;
         const uint16_t* ssl = reinterpret_cast<const uint16_t*>(wsl + a.slot_w);
@@ -349,11 +457,11 @@ __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const C
             const __half v = f2h(__fmul_rn(run, as));
             const int n = r + tid;
             if (epi == kEpiStore) {
-                out[n] = v;
+                st_tagged(out + n, v, tag_out);
             } else if (epi == kEpiResid) {
-                out[n] = __hadd(res, v);
+                st_tagged(out + n, __hadd(res, v), tag_out);
             } else if (epi == kEpiLm) {
-                out[n] = v;
+                lm_out[n] = v;
                 const unsigned long long key = argmax_key(h2f(v), n);
                 best = key > best ? key : best;
             } else {
@@ -363,44 +471,9 @@ __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const C
         cbar();
         if (tid == 0) mbar_arrive(&empty[s]);
         if (epi == kEpiGlu && tid < rows / 2)
-            out[(r >> 1) + tid] = __hmul(ref_silu(m.ob[2 * tid]), m.ob[2 * tid + 1]);
+            st_tagged(out + (r >> 1) + tid, __hmul(ref_silu(m.ob[2 * tid]), m.ob[2 * tid + 1]), tag_out);
     }
     return true;
-}
-
-// Number of blocks that own rows of an N-row job (8-row units split evenly over P blocks).
-__host__ __device__ inline int blocks_with_rows(int N, int P) { return (N >> 3) < P ? (N >> 3) : P; }
-
-// grid-wide barrier over the consumer warps of all blocks. Only the `narrive` blocks that wrote
-// data in the phase before it arrive (`arrive`); every block waits. The target is cumulative
-// (`tgt`), the same in every block; a block that does not arrive still passes every barrier in
-// order, so later barriers that it does arrive at order its reads before any later overwrite.
-__device__ __forceinline__ bool grid_sync(const PArgs& a, unsigned& tgt, int* flag, bool arrive, int narrive) {
-    cbar();
-    tgt += (unsigned)narrive;
-    if (threadIdx.x == 0) {
-        bool ok = !ld_volatile_u32(&a.sync->abort);
-        if (ok) {
-            // release: the block's writes (ordered before by the consumer barrier) become
-            // visible before the arrival
-            if (arrive) red_release_gpu_add(&a.sync->bar, 1u);
-            const unsigned target = tgt;
-            uint32_t i = 0;
-            // acquire loads: the observing load orders what follows, no separate fence (measured
-            // on B200 with 148 blocks: 1.40 us per barrier against 1.78 us for relaxed polling
-            // plus one acquire fence)
-            while (ld_acquire_gpu(&a.sync->bar) < target) {
-                if (++i > a.spin_limit || ((i & 63) == 0 && ld_volatile_u32(&a.sync->abort))) {
-                    ok = false;
-                    break;
-                }
-            }
-        }
-        if (!ok) set_abort(a, kDevFlagTimeout);
-        *flag = ok ? 1 : 0;
-    }
-    cbar();
-    return *flag != 0;
 }
 
 template <int D>
@@ -475,8 +548,11 @@ __device__ __forceinline__ void attention_prefetch(const PArgs& a, int l, int h,
     attn_stage_chunk<D, kPC, kACH>(c, awork, 0);  // commits the group (the copies above included)
 }
 
+// Attention of head h in layer l: waits for the head's q and its kv head's k / v rows
+// (tagged `tq`), writes its output rows tagged `ta`. False when a poll gave up.
 template <int D>
-__device__ __forceinline__ void attention_head(const PArgs& a, int l, int h, uint8_t* work, int cache_len, int total_len) {
+__device__ __forceinline__ bool attention_head(const PArgs& a, const Cs& m, int l, int h, uint8_t* work, int cache_len,
+                                               int total_len, unsigned tq, unsigned ta) {
     const int tid = threadIdx.x, warp = tid >> 5;
     const int grp = a.Hq / a.Hkv, kvh = h / grp;
     const int nqg = (D + 127) / 128;
@@ -488,13 +564,29 @@ __device__ __forceinline__ void attention_head(const PArgs& a, int l, int h, uin
     // memory clobbers, so a read placed after one would add an L2 round trip to the phase
     const AttnCoreArgs c = attn_args<D>(a, ly, h, cache_len, total_len, qs, kr, hv);
     const bool rope = ly.ct != nullptr, qnorm = ly.q_norm != nullptr, knorm = ly.k_norm != nullptr;
-    for (int d = tid; d < D; d += kPC) {
-        hq[d] = __ldcg(a.qkv + (size_t)h * D + d);
-        hk[d] = __ldcg(a.qkv + (size_t)(a.Hq + kvh) * D + d);
-        hv[d] = __ldcg(a.qkv + (size_t)(a.Hq + a.Hkv + kvh) * D + d);
+    static_assert(D <= kPC, "one thread per dim");
+    if (tid < D) {
+        // the three words are requested together; only the ones not yet written are re-polled
+        const uint32_t* pq = a.qkv + (size_t)h * D + tid;
+        const uint32_t* pk = a.qkv + (size_t)(a.Hq + kvh) * D + tid;
+        const uint32_t* pv = a.qkv + (size_t)(a.Hq + a.Hkv + kvh) * D + tid;
+        uint32_t wq = ld_relaxed_gpu(pq), wk = ld_relaxed_gpu(pk), wv = ld_relaxed_gpu(pv);
+        for (uint32_t it = 0; ((wq >> 16) != tq) | ((wk >> 16) != tq) | ((wv >> 16) != tq); ++it) {
+            if (!poll_go_on(a, it)) {
+                *m.fail = 1;
+                break;
+            }
+            if ((wq >> 16) != tq) wq = ld_relaxed_gpu(pq);
+            if ((wk >> 16) != tq) wk = ld_relaxed_gpu(pk);
+            if ((wv >> 16) != tq) wv = ld_relaxed_gpu(pv);
+        }
+        hq[tid] = word_h(wq);
+        hk[tid] = word_h(wk);
+        hv[tid] = word_h(wv);
     }
     cp_async_wait<0>();  // the prefetched norm weights / RoPE rows / K/V of this thread
     cbar();
+    if (*m.fail) return false;
     const __half* crow = rope ? sm.crow : nullptr;
     if (warp == 0) head_norm_rope_rows(hq, D, qnorm ? sm.qn : nullptr, a.eps, crow, sm.srow, qr);
     else if (warp == 1) head_norm_rope_rows(hk, D, knorm ? sm.kn : nullptr, a.eps, crow, sm.srow, kr);
@@ -513,12 +605,14 @@ __device__ __forceinline__ void attention_head(const PArgs& a, int l, int h, uin
     }
     cbar();
     const __half o = attn_exact_core<D, kPC, kACH>(c, work, SyncConsumers{});
-    if (tid < D) a.attn[(size_t)h * D + tid] = o;
+    if (tid < D) st_tagged(a.attn + (size_t)h * D + tid, o, ta);
+    return true;
 }
 
 // embedding row of `tok` (compute_embedding_node semantics, as embed_kernel) into xs; the
-// block also stores its slice of the hidden state
+// block also stores its slice of the hidden state (tagged version 0)
 __device__ __forceinline__ void embed_row(const PArgs& a, uint32_t tok, __half* xs) {
+    const unsigned tag = vtag(a, 0);
     const int H = a.H;
     const int k0 = (int)(((long long)H * blockIdx.x) / gridDim.x), k1 = (int)(((long long)H * (blockIdx.x + 1)) / gridDim.x);
     for (int k = threadIdx.x; k < H; k += kPC) {
@@ -537,7 +631,7 @@ __device__ __forceinline__ void embed_row(const PArgs& a, uint32_t tok, __half* 
             v = f2h(__fmul_rn((float)q, h2f(a.emb_s[(size_t)tok * (H / a.emb_G) + k / a.emb_G])));
         }
         xs[k] = v;
-        if (k >= k0 && k < k1) a.hidden[k] = v;
+        if (k >= k0 && k < k1) st_tagged(a.hidden + k, v, tag);
     }
     cbar();
 }
@@ -547,7 +641,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[64];
     __shared__ float s_as;
-    __shared__ int s_flag;
+    __shared__ int s_flag, s_fail;
     __shared__ unsigned long long s_best[16];
     const int NS = a.nslots, sb = a.slot_w + a.slot_s;
     uint8_t* ring = smem;
@@ -556,6 +650,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     uint8_t* work = smem + (size_t)NS * sb + a128(16 * NS);
     const int tid = threadIdx.x;
     if (tid == 0) {
+        s_fail = 0;
         s_flag = ld_volatile_u32(&a.sync->abort) ? 0 : 1;
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
@@ -579,22 +674,14 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     m.red = s_red;
     m.as = &s_as;
     m.flag = &s_flag;
+    m.fail = &s_fail;
     m.best = s_best;
 
     const int cache_len = __ldcg(a.state), total_len = __ldcg(a.state + 1);
     const uint32_t tok = __ldcg(a.tok_in);
     uint8_t* awork = work + a.attn_off;
     const bool attn_block = (int)blockIdx.x < a.Hq;
-    unsigned kslot = 0, tgt = 0;
-    const int P = gridDim.x, c = blockIdx.x;
-    int rr0, rr1;
-    rows_of(a.H, c, P, rr0, rr1);
-    const bool rows_h = rr1 > rr0;                 // rows of O and down (N = H)
-    rows_of(a.QKVN, c, P, rr0, rr1);
-    const bool rows_qkv = rr1 > rr0;
-    rows_of(2 * a.F, c, P, rr0, rr1);
-    const bool rows_gu = rr1 > rr0;
-    const int n_qkv = blocks_with_rows(a.QKVN, P), n_h = blocks_with_rows(a.H, P), n_gu = blocks_with_rows(2 * a.F, P);
+    unsigned kslot = 0;
     unsigned long long best = 0ull;
     embed_row(a, tok, m.xs);
     // attention blocks stage layer 0's cached K/V rows (later layers: at the end of the layer
@@ -607,31 +694,34 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
         const __half* const in_norm = ly.in_norm;
         const __half* const post_norm = ly.post_norm;
         const int4 nw_in = norm_chunk(in_norm, a.H), nw_post = norm_chunk(post_norm, a.H);
-        load_vec(m, l > 0 ? a.hidden : nullptr, a.H, true);
+        // versions: the hidden state entering the layer 5 l (the embedding, or the previous
+        // layer's down projection), then QKV, attention, O, gate-up, down
+        const unsigned t_in = vtag(a, 5 * l), t_qkv = vtag(a, 5 * l + 1), t_att = vtag(a, 5 * l + 2),
+                       t_o = vtag(a, 5 * l + 3), t_gu = vtag(a, 5 * l + 4), t_dn = vtag(a, 5 * l + 5);
+        if (l > 0) {
+            if (!load_tagged(m, a, a.hidden, a.H, t_in, true)) return;
+        } else {
+            load_vec(m, nullptr, a.H, true);  // xs holds the embedding row
+        }
         prologue(m, a.H, in_norm, a.eps, nw_in);
-        if (!gemv_job(a, 4 * l, kEpiStore, m, ring, full, empty, kslot, a.qkv, best)) return;
-        if (!grid_sync(a, tgt, m.flag, rows_qkv, n_qkv)) return;
-        if (attn_block) attention_head<D>(a, l, blockIdx.x, awork, cache_len, total_len);
-        if (!grid_sync(a, tgt, m.flag, attn_block, a.Hq)) return;
-        load_vec(m, a.attn, a.Hq * D, false);
+        if (!gemv_job(a, 4 * l, kEpiStore, m, ring, full, empty, kslot, a.qkv, nullptr, t_qkv, 0u, best)) return;
+        if (attn_block && !attention_head<D>(a, m, l, blockIdx.x, awork, cache_len, total_len, t_qkv, t_att)) return;
+        if (!load_tagged(m, a, a.attn, a.Hq * D, t_att, false)) return;
         prologue(m, a.Hq * D, nullptr, a.eps, make_int4(0, 0, 0, 0));
-        if (!gemv_job(a, 4 * l + 1, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
-        if (!grid_sync(a, tgt, m.flag, rows_h, n_h)) return;
-        load_vec(m, a.hidden, a.H, true);
+        if (!gemv_job(a, 4 * l + 1, kEpiResid, m, ring, full, empty, kslot, a.hidden, nullptr, t_o, t_in, best)) return;
+        if (!load_tagged(m, a, a.hidden, a.H, t_o, true)) return;
         prologue(m, a.H, post_norm, a.eps, nw_post);
-        if (!gemv_job(a, 4 * l + 2, kEpiGlu, m, ring, full, empty, kslot, a.gated, best)) return;
-        if (!grid_sync(a, tgt, m.flag, rows_gu, n_gu)) return;
-        load_vec(m, a.gated, a.F, false);
+        if (!gemv_job(a, 4 * l + 2, kEpiGlu, m, ring, full, empty, kslot, a.gated, nullptr, t_gu, 0u, best)) return;
+        if (!load_tagged(m, a, a.gated, a.F, t_gu, false)) return;
         prologue(m, a.F, nullptr, a.eps, make_int4(0, 0, 0, 0));
-        if (!gemv_job(a, 4 * l + 3, kEpiResid, m, ring, full, empty, kslot, a.hidden, best)) return;
+        if (!gemv_job(a, 4 * l + 3, kEpiResid, m, ring, full, empty, kslot, a.hidden, nullptr, t_dn, t_o, best)) return;
         // the next layer's cache rows are fixed for this token and the staging area is free
         if (attn_block && l + 1 < a.L) attention_prefetch<D>(a, l + 1, blockIdx.x, awork, cache_len, total_len);
-        if (!grid_sync(a, tgt, m.flag, rows_h, n_h)) return;
     }
     const int4 nw_out = norm_chunk(a.out_norm, a.H);
-    load_vec(m, a.hidden, a.H, true);
+    if (!load_tagged(m, a, a.hidden, a.H, vtag(a, 5 * a.L), true)) return;
     prologue(m, a.H, a.out_norm, a.eps, nw_out);
-    if (!gemv_job(a, 4 * a.L, kEpiLm, m, ring, full, empty, kslot, a.logits, best)) return;
+    if (!gemv_job(a, 4 * a.L, kEpiLm, m, ring, full, empty, kslot, nullptr, a.logits, 0u, 0u, best)) return;
     // block first-max, then the last block to finish picks the token
     for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, best, o);
@@ -656,7 +746,6 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
             a.state[1] = total_len + 1;
             a.state[2] = step + 1;
             a.sync->key = 0ull;
-            a.sync->bar = 0u;
             a.sync->done = 0u;
             __threadfence();
         }
@@ -678,7 +767,11 @@ PPlan persistent_plan(PArgs& a, int num_sms, size_t smem_optin) {
         return p;
     };
     if (a.D != 64 && a.D != 128) return no("head_dim must be 64 or 128");
-    if (a.Hq > num_sms || a.Hkv < 1 || a.Hq % a.Hkv) return no("head layout");
+    // every block must own rows of the QKV and gate-up projections (the tagged hand-over
+    // relies on it to order buffer reuse), so small models run on fewer blocks
+    const int grid = std::min(num_sms, std::min(a.QKVN >> 3, a.F >> 2));
+    if (a.Hq > grid || a.Hkv < 1 || a.Hq % a.Hkv) return no("head layout");
+    if (ptag_span(a.L) >= 65535u) return no("too many layers for the 16-bit version tags");
     if (a.G < 16 || a.G % 16 || 32 % (a.G / 16)) return no("group size");
     const int Ks[3] = {a.H, a.Hq * a.D, a.F};
     int kmin = Ks[0], kmax = Ks[0];
@@ -721,7 +814,7 @@ PPlan persistent_plan(PArgs& a, int num_sms, size_t smem_optin) {
     if (NS < 2) return no("shared memory too small for two weight slots");
     a.nslots = NS;
     p.smem = (size_t)NS * sb + a128(16 * NS) + a.work_bytes;
-    p.grid = num_sms;
+    p.grid = grid;
     p.threads = kPT;
     p.ok = true;
     return p;

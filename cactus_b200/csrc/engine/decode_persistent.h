@@ -20,11 +20,19 @@ struct PLayer {
 };
 
 // Device-resident synchronisation words. Zero before the first launch of a run; the last
-// block of every launch zeroes bar/done/key again. `abort` stays set after a failure.
+// block of every launch zeroes done/key again. `abort` stays set after a failure.
 struct PSync {
-    unsigned bar, done, abort, pad;
+    unsigned done, abort, pad0, pad1;
     unsigned long long key;
 };
+
+// Activations that cross blocks travel as tagged words: the fp16 bits in the low half and the
+// writer's 16-bit version tag in the high half. A reader polls the words it needs until they
+// carry the version it expects, so the data is its own ready flag and no grid barrier is
+// needed. Version v of a launch (v = 0 for the embedding, 5 l + 1 .. 5 l + 5 for layer l's
+// QKV, attention, O, gate-up and down outputs) has tag 1 + (tag_base + v) % 65535: never 0
+// (the buffers start zeroed), and the host advances tag_base by ptag_span(L) per launch.
+__host__ __device__ inline unsigned ptag_span(int L) { return 5u * (unsigned)L + 1u; }
 
 struct PArgs {
     const PLayer* layers;
@@ -36,7 +44,9 @@ struct PArgs {
     const __half* emb_s;
     int emb_prec, emb_G;
     float eps, attn_scale;
-    __half *hidden, *qkv, *attn, *gated, *logits;  // [H], [QKVN], [Hq*D], [F], [V]
+    uint32_t *hidden, *qkv, *attn, *gated;  // tagged words: [H], [QKVN], [Hq*D], [F]
+    __half* logits;                         // [V]
+    unsigned tag_base;                      // this launch's tag offset (see ptag_span)
     uint32_t* tok_in;       // input token of the step; the next token is written back here
     uint32_t* ring;         // optional: ring[state[2]] = next token
     int* state;             // [cache_len, total_len, step], advanced by the kernel

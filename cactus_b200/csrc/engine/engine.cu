@@ -378,6 +378,9 @@ void Engine::setup_persistent() {
     d_players_ = static_cast<PLayer*>(dmalloc(sizeof(PLayer) * L_, owned_));
     ck(cudaMemcpy(d_players_, pl.data(), sizeof(PLayer) * L_, cudaMemcpyHostToDevice), "persistent layers");
     psync_ = static_cast<PSync*>(dmalloc(sizeof(PSync), owned_));
+    ptagged_words_ = (size_t)H_ + QKVN_ + (size_t)Hq_ * D_ + F_;
+    ptagged_ = static_cast<uint32_t*>(dmalloc(ptagged_words_ * 4, owned_));
+    ck(cudaMemset(ptagged_, 0, ptagged_words_ * 4), "persistent activations");
     PArgs& a = pargs_;
     a = PArgs{};
     a.layers = d_players_;
@@ -391,7 +394,11 @@ void Engine::setup_persistent() {
     a.emb_G = embed_.G;
     a.eps = cfg_.layer_norm_eps;
     a.attn_scale = attention_scale_;
-    a.hidden = hidden_, a.qkv = qkv_, a.attn = attn_, a.gated = gated_, a.logits = logits_;
+    a.hidden = ptagged_;
+    a.qkv = a.hidden + H_;
+    a.attn = a.qkv + QKVN_;
+    a.gated = a.attn + (size_t)Hq_ * D_;
+    a.logits = logits_;
     a.tok_in = tok_in_;
     a.state = dstate_;
     a.sync = psync_;
@@ -907,7 +914,11 @@ void Engine::generate(const uint32_t* prompts, int B, size_t P, size_t max_new, 
     if (can_persist) {
         pargs_.ring = ring_;
         ck(cudaMemsetAsync(psync_, 0, sizeof(PSync), stream_), "persistent sync");
-        for (; step < max_new; ++step) ck(launch_persistent_decode(pargs_, pplan_, stream_), "persistent decode");
+        for (; step < max_new; ++step) {
+            pargs_.tag_base = ptag_base_;  // every launch writes new versions of the tagged words
+            ptag_base_ = (ptag_base_ + ptag_span(L_)) % 65535u;
+            ck(launch_persistent_decode(pargs_, pplan_, stream_), "persistent decode");
+        }
         cache_len_ += max_new;
         total_len_ += max_new;
         launches_ += (long long)max_new;
@@ -974,7 +985,11 @@ void Engine::generate(const uint32_t* prompts, int B, size_t P, size_t max_new, 
     if (last_path_ == 2) {
         PSync ps;
         ck(cudaMemcpy(&ps, psync_, sizeof(ps), cudaMemcpyDeviceToHost), "persistent sync");
-        if (ps.abort) throw std::runtime_error("persistent decode step gave up a bounded wait (device error recorded)");
+        if (ps.abort) {
+            // words of the abandoned launch must not pass for a later version
+            ck(cudaMemset(ptagged_, 0, ptagged_words_ * 4), "persistent activations");
+            throw std::runtime_error("persistent decode step gave up a bounded wait (device error recorded)");
+        }
     }
     float a = 0, b = 0;
     ck(cudaEventElapsedTime(&a, ev_[0], ev_[1]), "elapsed");

@@ -180,6 +180,9 @@ private:
     PPlan pplan_;
     PLayer* d_players_ = nullptr;
     PSync* psync_ = nullptr;
+    uint32_t* ptagged_ = nullptr;  // the persistent step's tagged activation words (zeroed)
+    size_t ptagged_words_ = 0;
+    unsigned ptag_base_ = 0;       // advanced by ptag_span(L) per persistent launch
 };
 
 }  // namespace eng

@@ -201,10 +201,10 @@ def test_persistent_decode_matches_graph_path_and_oracle(tmp_path_factory, kind)
 def test_bounded_waits_give_up_and_the_next_call_succeeds(tmp_path_factory):
     """Every wait of the persistent decode step is bounded. With the bound lowered to one poll
     (CACTUS_B200_SPIN_LIMIT, read when an engine is created) the first wait on a weight slot or
-    a grid barrier gives up: the step raises the abort word, every block leaves at its next
-    wait (the producer after its copies in flight land), the call reports the failure and the
-    device error word records it. Nothing faults; an engine created afterwards decodes
-    normally in the same process."""
+    on another block's tagged activations gives up: the step raises the abort word, every block
+    leaves at its next wait (the producer after its copies in flight land), the call reports
+    the failure and the device error word records it. Nothing faults; an engine created
+    afterwards decodes normally in the same process."""
     import cactus_b200 as cb
     folder = convert.make_model(str(tmp_path_factory.mktemp("spin")), PERSISTENT_KINDS["qwen"](), seed=4,
                                 norm_std=0.1)
@@ -220,7 +220,7 @@ def test_bounded_waits_give_up_and_the_next_call_succeeds(tmp_path_factory):
         eng.close()
     finally:
         del os.environ["CACTUS_B200_SPIN_LIMIT"]
-    assert L.cactus_cuda_device_error(None) in (1, 2)  # a slot (TMA) or barrier (flag) timeout
+    assert L.cactus_cuda_device_error(None) in (1, 2)  # a slot (TMA) or tagged-word (flag) timeout
     assert L.cactus_cuda_device_error(None) == 0       # reading it cleared it
     eng = Engine(folder, context_size=512)
     got = eng.generate_greedy(prompt, 8).tolist()
