@@ -35,7 +35,7 @@ __host__ __device__ constexpr int attn_krow() {
 // shared-memory footprint of attn_exact_core<D, CH> (a multiple of 16 bytes)
 template <int D, int CH>
 __host__ __device__ constexpr int attn_core_smem() {
-    return CH * attn_krow<D>() + CH * D + (CH * 2 * 2 + 2 * CH + 4 * (CH / 32)) * 4;
+    return CH * attn_krow<D>() + CH * D + (CH * 2 * 2 + 2 * CH + 3 * (CH / 32)) * 4;
 }
 
 struct SyncBlock {
@@ -105,7 +105,6 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
     float* bmx = sw + CH;                               // [CH/32] block maxima
     float* bsm = bmx + CH / 32;                         // [CH/32] block sums
     float* bcorr = bsm + CH / 32;                       // [CH/32] running-max corrections
-    int* bzf = reinterpret_cast<int*>(bcorr + CH / 32); // [CH/32] 1: the block has a zero weight
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const float* qs = a.qs;
     const int vg = t < D ? t / a.qgs : 0;  // V scale group of this thread's dim
@@ -140,11 +139,12 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
                     for (int d = kj; d < D; d += 8) acc8 = fmaf(qs[d], h2f(kr[d]), acc8);
                 }
             }
-            const int base = lane & ~7;
-            float p[8];
-#pragma unroll
-            for (int m = 0; m < 8; ++m) p[m] = __shfl_sync(0xffffffffu, acc8, base + m);
-            float s = __fmul_rn(fold8(p), a.scale);
+            // fold8's tree as a butterfly on the 8 lanes of the key: ((l0 + l4) + (l1 + l5)) +
+            // ((l2 + l6) + (l3 + l7)), complete in lane kj = 0
+            const float f4 = __fadd_rn(acc8, __shfl_down_sync(0xffffffffu, acc8, 4));
+            const float f1 = __fadd_rn(f4, __shfl_down_sync(0xffffffffu, f4, 1));
+            const float f2 = __fadd_rn(f1, __shfl_down_sync(0xffffffffu, f1, 2));
+            float s = __fmul_rn(f2, a.scale);
             if (i >= n || (a.causal && c0 + i > a.aq)) s = -INFINITY;
             if (kj == 0 && i < CH) sc[i] = s;
         }
@@ -171,17 +171,21 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
                 }
             }
             const float corr = expf_cr(__fsub_rn(pm, m));
-            float sum = 0.0f;
-#pragma unroll
-            for (int l = 0; l < 32; ++l) {
-                const float x = __shfl_sync(0xffffffffu, w, l);
-                if (l < bs) sum = __fadd_rn(sum, x);
-            }
-            const unsigned zero = __ballot_sync(0xffffffffu, lane < bs && w == 0.0f);
+            __syncwarp();
             if (lane == 0) {
+                // the block's in-order weight sum from shared memory (16-byte loads)
+                const float4* w4 = reinterpret_cast<const float4*>(sw + warp * 32);
+                float sum = 0.0f;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 x = w4[q];
+                    if (4 * q < bs) sum = __fadd_rn(sum, x.x);
+                    if (4 * q + 1 < bs) sum = __fadd_rn(sum, x.y);
+                    if (4 * q + 2 < bs) sum = __fadd_rn(sum, x.z);
+                    if (4 * q + 3 < bs) sum = __fadd_rn(sum, x.w);
+                }
                 bmx[warp] = m;
                 bsm[warp] = sum;
-                bzf[warp] = zero ? 1 : 0;
                 bcorr[warp] = corr;
             }
         }
@@ -196,60 +200,45 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
                 run_max = m;
             }
             if (t < D) {
-                // keys with weight 0 leave acc untouched (the reference skips them); a select
-                // keeps the loop branch-free so the loads of a block pipeline
+                // keys with weight 0 leave acc untouched (the reference skips them). A plain fmaf
+                // does the same: v is finite, so v * (+0) is a signed zero, and acc is never -0
+                // (it starts at +0, a product of zero adds +0 or -0 to +0 giving +0, an exact
+                // cancellation rounds to +0, and scaling keeps the sign), so acc + (+-0) == acc.
                 const int i0 = blk * 32, i1 = min(n, i0 + 32);
-                const int ic = min(i1, max(i0, ncached));  // [i0, ic) cached, [ic, i1) new keys
-                const float* vs_t = vsc + vg;
-                if (ic - i0 == 32 && !bzf[blk]) {
-                    // no zero weight in the block: 16-byte weight / scale loads, the values of 16
-                    // keys dequantised ahead, then the plain fmaf chain (same operations)
-                    const float4* w4 = reinterpret_cast<const float4*>(sw + i0);
-                    const float4* s4 = reinterpret_cast<const float4*>(vsc + i0 * 2);
+                const int nc = min(i1, max(i0, ncached)) - i0;  // [i0, i0 + nc) cached, then new keys
+                // 16-byte weight / scale loads, the values of 16 keys dequantised ahead, then the
+                // fmaf chain in key order (rows past the cached ones are staged memory, unused)
+                const float4* w4 = reinterpret_cast<const float4*>(sw + i0);
+                const float4* s4 = reinterpret_cast<const float4*>(vsc + i0 * 2);
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float v[16], w[16];
+                for (int h = 0; h < 2; ++h) {
+                    float v[16], w[16];
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const float4 q = w4[4 * h + j];
-                            w[4 * j] = q.x;
-                            w[4 * j + 1] = q.y;
-                            w[4 * j + 2] = q.z;
-                            w[4 * j + 3] = q.w;
-                        }
+                    for (int j = 0; j < 4; ++j) {
+                        const float4 q = w4[4 * h + j];
+                        w[4 * j] = q.x;
+                        w[4 * j + 1] = q.y;
+                        w[4 * j + 2] = q.z;
+                        w[4 * j + 3] = q.w;
+                    }
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const float4 q = s4[8 * h + j];  // scales of keys 2j, 2j + 1: [key][2]
-                            const int i = i0 + 16 * h + 2 * j;
-                            v[2 * j] = __fmul_rn(i2f_small(vraw[i * D + t]), vg ? q.y : q.x);
-                            v[2 * j + 1] = __fmul_rn(i2f_small(vraw[(i + 1) * D + t]), vg ? q.w : q.z);
-                        }
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 q = s4[8 * h + j];  // scales of keys 2j, 2j + 1: [key][2]
+                        const int i = i0 + 16 * h + 2 * j;
+                        v[2 * j] = __fmul_rn(i2f_small(vraw[i * D + t]), vg ? q.y : q.x);
+                        v[2 * j + 1] = __fmul_rn(i2f_small(vraw[(i + 1) * D + t]), vg ? q.w : q.z);
+                    }
+                    if (nc == 32) {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) acc = fmaf(v[j], w[j], acc);
-                    }
-                } else if (ic - i0 == 32) {
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int i = i0 + j;
-                        const float w = sw[i];
-                        const float v = __fmul_rn(i2f_small(vraw[i * D + t]), vs_t[i * 2]);
-                        const float nacc = fmaf(v, w, acc);
-                        acc = (w == 0.0f) ? acc : nacc;
-                    }
-                } else {
-                    for (int i = i0; i < ic; ++i) {
-                        const float w = sw[i];
-                        const float v = __fmul_rn((float)vraw[i * D + t], vs_t[i * 2]);
-                        const float nacc = fmaf(v, w, acc);
-                        acc = (w == 0.0f) ? acc : nacc;
+                        for (int j = 0; j < 16; ++j)
+                            if (16 * h + j < nc) acc = fmaf(v[j], w[j], acc);
                     }
                 }
-                for (int i = ic; i < i1; ++i) {
-                    const float w = sw[i];
-                    const float v = h2f(a.Vn[(size_t)(c0 + i - a.cache_len) * a.kn_row + t]);
-                    const float nacc = fmaf(v, w, acc);
-                    acc = (w == 0.0f) ? acc : nacc;
-                }
+                for (int i = i0 + nc; i < i1; ++i)
+                    acc = fmaf(h2f(a.Vn[(size_t)(c0 + i - a.cache_len) * a.kn_row + t]), sw[i], acc);
             }
             run_sum = __fadd_rn(run_sum, bsm[blk]);
         }
