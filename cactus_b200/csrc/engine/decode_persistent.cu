@@ -20,7 +20,19 @@
 //    and a phase starts as soon as its own inputs exist (the attention blocks wait for their
 //    head's rows only). Reuse of a buffer is ordered by the data flow: every block writes
 //    QKV and gate-up rows (the grid is sized so), and every reader waits for whole vectors,
-//    so a block can only overwrite a version once every block has read it.
+//    so a block can only overwrite a version once every block has read it. Per buffer:
+//    - hidden (O / down outputs, read whole by the next RMSNorm prologue): a down writer has
+//      read all of `gated`, which every block wrote after reading the O version; an O writer
+//      has read all of `attn`, whose heads needed every QKV row, which every block wrote
+//      after reading the down version. The residual reads are the writer's own rows.
+//    - qkv: a writer has read the whole hidden state of the previous down phase, whose
+//      writers read all of `gated`, written by every block after its attention work.
+//    - attn: a head's writer read its QKV rows, written after their blocks read the whole
+//      hidden state, i.e. after all of `gated` of the previous layer, which every block
+//      wrote after its O prologue had read `attn`.
+//    - gated: a writer read the whole O output, whose writers read all of `attn`, whose
+//      heads waited for QKV rows that every block wrote after its down prologue of the
+//      previous layer had read `gated`.
 //  * blocks 0..Hq-1 run one attention head each (the reference-order core).
 //  * the lm head keeps a per-block first-max key; the last block to finish combines them,
 //    writes the next token, advances the device state and re-arms the sync words.
