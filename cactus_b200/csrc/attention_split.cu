@@ -118,15 +118,24 @@ __global__ void __launch_bounds__(kS1Threads) attn_split_scores_kernel(SplitArgs
     const int* pt = a.pg.table ? a.pg.table + (size_t)b * a.pg.pps : nullptr;
     const int8_t* Kc = a.kc + (pt ? 0 : b * a.kc_bstride) + (size_t)kvh * D;
     const float* ks = a.ks + (pt ? 0 : b * a.sc_bstride) + (size_t)kvh * nqg;
-    for (int c = t; c < ncached * (D / 16); c += kS1Threads) {
-        const int i = c / (D / 16), off = (c % (D / 16)) * 16;
-        const long long row = pt ? kv_page_row(pt, a.pg.shift, c0 + i) : c0 + i;
-        cp_async16(kraw + i * KR + off, Kc + (size_t)row * kv_row + off);
-    }
-    for (int c = t; c < ncached * nqg; c += kS1Threads) {
-        const int i = c / nqg, g = c % nqg;
-        const long long row = pt ? kv_page_row(pt, a.pg.shift, c0 + i) : c0 + i;
-        cp_async4(ksc + i * 2 + g, ks + (size_t)row * sc_row + g);
+    if (pt) {  // paged: rows through the block table (the branch is uniform, outside the loops)
+        for (int c = t; c < ncached * (D / 16); c += kS1Threads) {
+            const int i = c / (D / 16), off = (c % (D / 16)) * 16;
+            cp_async16(kraw + i * KR + off, Kc + (size_t)kv_page_row(pt, a.pg.shift, c0 + i) * kv_row + off);
+        }
+        for (int c = t; c < ncached * nqg; c += kS1Threads) {
+            const int i = c / nqg, g = c % nqg;
+            cp_async4(ksc + i * 2 + g, ks + (size_t)kv_page_row(pt, a.pg.shift, c0 + i) * sc_row + g);
+        }
+    } else {
+        for (int c = t; c < ncached * (D / 16); c += kS1Threads) {
+            const int i = c / (D / 16), off = (c % (D / 16)) * 16;
+            cp_async16(kraw + i * KR + off, Kc + (size_t)(c0 + i) * kv_row + off);
+        }
+        for (int c = t; c < ncached * nqg; c += kS1Threads) {
+            const int i = c / nqg, g = c % nqg;
+            cp_async4(ksc + i * 2 + g, ks + (size_t)(c0 + i) * sc_row + g);
+        }
     }
     cp_async_commit();
     const int h0 = kvh * grp;
@@ -250,15 +259,24 @@ __global__ void __launch_bounds__(s2_dims<D>()) attn_split_chain_kernel(SplitArg
         const long long c0 = c * kS2Keys;
         const int n = (int)min((long long)kS2Keys, kv_end - c0);
         const int ncached = (int)max(0LL, min((long long)n, (long long)a.cache_len - c0));
-        for (int x = t; x < ncached * (DC / 16); x += DC) {
-            const int i = x / (DC / 16), off = (x % (DC / 16)) * 16;
-            const long long row = pt ? kv_page_row(pt, a.pg.shift, c0 + i) : c0 + i;
-            cp_async16(vraw + i * DC + off, Vc + (size_t)row * kv_row + dim0 + off);
-        }
-        for (int x = t; x < ncached * nqg; x += DC) {
-            const int i = x / nqg, g = x % nqg;
-            const long long row = pt ? kv_page_row(pt, a.pg.shift, c0 + i) : c0 + i;
-            cp_async4(vsc + g * kS2Keys + i, vs + (size_t)row * sc_row + g);
+        if (pt) {  // paged: rows through the block table (uniform branch, outside the loops)
+            for (int x = t; x < ncached * (DC / 16); x += DC) {
+                const int i = x / (DC / 16), off = (x % (DC / 16)) * 16;
+                cp_async16(vraw + i * DC + off, Vc + (size_t)kv_page_row(pt, a.pg.shift, c0 + i) * kv_row + dim0 + off);
+            }
+            for (int x = t; x < ncached * nqg; x += DC) {
+                const int i = x / nqg, g = x % nqg;
+                cp_async4(vsc + g * kS2Keys + i, vs + (size_t)kv_page_row(pt, a.pg.shift, c0 + i) * sc_row + g);
+            }
+        } else {
+            for (int x = t; x < ncached * (DC / 16); x += DC) {
+                const int i = x / (DC / 16), off = (x % (DC / 16)) * 16;
+                cp_async16(vraw + i * DC + off, Vc + (size_t)(c0 + i) * kv_row + dim0 + off);
+            }
+            for (int x = t; x < ncached * nqg; x += DC) {
+                const int i = x / nqg, g = x % nqg;
+                cp_async4(vsc + g * kS2Keys + i, vs + (size_t)(c0 + i) * sc_row + g);
+            }
         }
         for (int x = t; x < n; x += DC) cp_async4(wst + x, W + c0 + x);
         cp_async_commit();
