@@ -699,41 +699,42 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     // attention blocks stage layer 0's cached K/V rows (later layers: at the end of the layer
     // before, off the critical path of the QKV phase)
     if (attn_block) attention_prefetch<D>(a, 0, blockIdx.x, awork, cache_len, total_len);
-    for (int l = 0; l < a.L; ++l) {
-        const PLayer& ly = a.layers[l];
-        // norm pointers in registers: reads of `ly` after a block barrier (a memory clobber)
-        // would be repeated as L2 round trips
-        const __half* const in_norm = ly.in_norm;
-        const __half* const post_norm = ly.post_norm;
-        const int4 nw_in = norm_chunk(in_norm, a.H), nw_post = norm_chunk(post_norm, a.H);
-        // versions: the hidden state entering the layer 5 l (the embedding, or the previous
-        // layer's down projection), then QKV, attention, O, gate-up, down
-        const unsigned t_in = vtag(a, 5 * l), t_qkv = vtag(a, 5 * l + 1), t_att = vtag(a, 5 * l + 2),
-                       t_o = vtag(a, 5 * l + 3), t_gu = vtag(a, 5 * l + 4), t_dn = vtag(a, 5 * l + 5);
-        if (l > 0) {
-            if (!load_tagged(m, a, a.hidden, a.H, t_in, true)) return;
+    // One loop over the projection jobs (j = 4 l + {QKV, O, gate-up, down}, then the lm head)
+    // with the phase-specific values selected at run time: the input / prologue / GEMV code
+    // exists once in the kernel instead of once per phase, which keeps the instruction
+    // footprint of the hot loop small.
+    // Versions of the tagged words: the hidden state entering layer l is 5 l (the embedding,
+    // or the previous layer's down projection), then QKV 5 l + 1, attention + 2, O + 3,
+    // gate-up + 4, down + 5.
+    for (int j = 0; j <= 4 * a.L; ++j) {
+        const int l = j >> 2, p = j & 3;
+        const bool lm = j == 4 * a.L;
+        const __half* norm = nullptr;
+        if (lm) norm = a.out_norm;
+        else if (p == 0) norm = a.layers[l].in_norm;
+        else if (p == 2) norm = a.layers[l].post_norm;
+        const int4 nw = norm_chunk(norm, a.H);
+        const uint32_t* src = p == 1 ? a.attn : (p == 3 ? a.gated : a.hidden);
+        const int K = p == 1 ? a.Hq * D : (p == 3 ? a.F : a.H);
+        const bool hid = p == 0 || p == 2;  // the hidden state (lane-major copy for the RMS chain)
+        const int vin = 5 * l + (p == 0 ? 0 : p == 1 ? 2 : p == 2 ? 3 : 4);
+        if (j > 0) {
+            if (!load_tagged(m, a, src, K, vtag(a, vin), hid)) return;
         } else {
             load_vec(m, nullptr, a.H, true);  // xs holds the embedding row
         }
-        prologue(m, a.H, in_norm, a.eps, nw_in);
-        if (!gemv_job(a, 4 * l, kEpiStore, m, ring, full, empty, kslot, a.qkv, nullptr, t_qkv, 0u, best)) return;
-        if (attn_block && !attention_head<D>(a, m, l, blockIdx.x, awork, cache_len, total_len, t_qkv, t_att)) return;
-        if (!load_tagged(m, a, a.attn, a.Hq * D, t_att, false)) return;
-        prologue(m, a.Hq * D, nullptr, a.eps, make_int4(0, 0, 0, 0));
-        if (!gemv_job(a, 4 * l + 1, kEpiResid, m, ring, full, empty, kslot, a.hidden, nullptr, t_o, t_in, best)) return;
-        if (!load_tagged(m, a, a.hidden, a.H, t_o, true)) return;
-        prologue(m, a.H, post_norm, a.eps, nw_post);
-        if (!gemv_job(a, 4 * l + 2, kEpiGlu, m, ring, full, empty, kslot, a.gated, nullptr, t_gu, 0u, best)) return;
-        if (!load_tagged(m, a, a.gated, a.F, t_gu, false)) return;
-        prologue(m, a.F, nullptr, a.eps, make_int4(0, 0, 0, 0));
-        if (!gemv_job(a, 4 * l + 3, kEpiResid, m, ring, full, empty, kslot, a.hidden, nullptr, t_dn, t_o, best)) return;
+        prologue(m, K, norm, a.eps, nw);
+        const int epi = lm ? kEpiLm : (p == 0 ? kEpiStore : p == 2 ? kEpiGlu : kEpiResid);
+        uint32_t* out = lm ? nullptr : (p == 0 ? a.qkv : p == 2 ? a.gated : a.hidden);
+        const unsigned t_out = vtag(a, 5 * l + (p == 0 ? 1 : p == 1 ? 3 : p == 2 ? 4 : 5));
+        const unsigned t_res = vtag(a, 5 * l + (p == 1 ? 0 : 3));  // O / down: the residual's version
+        if (!gemv_job(a, j, epi, m, ring, full, empty, kslot, out, a.logits, t_out, t_res, best)) return;
+        if (p == 0 && !lm && attn_block &&
+            !attention_head<D>(a, m, l, blockIdx.x, awork, cache_len, total_len, t_out, vtag(a, 5 * l + 2)))
+            return;
         // the next layer's cache rows are fixed for this token and the staging area is free
-        if (attn_block && l + 1 < a.L) attention_prefetch<D>(a, l + 1, blockIdx.x, awork, cache_len, total_len);
+        if (p == 3 && attn_block && l + 1 < a.L) attention_prefetch<D>(a, l + 1, blockIdx.x, awork, cache_len, total_len);
     }
-    const int4 nw_out = norm_chunk(a.out_norm, a.H);
-    if (!load_tagged(m, a, a.hidden, a.H, vtag(a, 5 * a.L), true)) return;
-    prologue(m, a.H, a.out_norm, a.eps, nw_out);
-    if (!gemv_job(a, 4 * a.L, kEpiLm, m, ring, full, empty, kslot, nullptr, a.logits, 0u, 0u, best)) return;
     // block first-max, then the last block to finish picks the token
     for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, best, o);
