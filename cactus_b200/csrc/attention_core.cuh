@@ -228,14 +228,9 @@ __device__ __forceinline__ __half attn_exact_core(const AttnCoreArgs& a, uint8_t
                         v[2 * j] = __fmul_rn(i2f_small(vraw[i * D + t]), vg ? q.y : q.x);
                         v[2 * j + 1] = __fmul_rn(i2f_small(vraw[(i + 1) * D + t]), vg ? q.w : q.z);
                     }
-                    if (nc == 32) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) acc = fmaf(v[j], w[j], acc);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            if (16 * h + j < nc) acc = fmaf(v[j], w[j], acc);
-                    }
+                    for (int j = 0; j < 16; ++j)
+                        if (16 * h + j < nc) acc = fmaf(v[j], w[j], acc);
                 }
                 for (int i = i0 + nc; i < i1; ++i)
                     acc = fmaf(h2f(a.Vn[(size_t)(c0 + i - a.cache_len) * a.kn_row + t]), sw[i], acc);

@@ -600,8 +600,11 @@ __device__ __forceinline__ bool attention_head(const PArgs& a, const Cs& m, int 
     cbar();
     if (*m.fail) return false;
     const __half* crow = rope ? sm.crow : nullptr;
-    if (warp == 0) head_norm_rope_rows(hq, D, qnorm ? sm.qn : nullptr, a.eps, crow, sm.srow, qr);
-    else if (warp == 1) head_norm_rope_rows(hk, D, knorm ? sm.kn : nullptr, a.eps, crow, sm.srow, kr);
+    if (warp < 2) {  // warp 0: q, warp 1: k (one inlined copy of the routine)
+        const bool isq = warp == 0;
+        head_norm_rope_rows(isq ? hq : hk, D, isq ? (qnorm ? sm.qn : nullptr) : (knorm ? sm.kn : nullptr), a.eps,
+                            crow, sm.srow, isq ? qr : kr);
+    }
     cbar();
     for (int d = tid; d < D; d += kPC) qs[d] = h2f(qr[d]);
     // the first q head of each group appends the step's K/V to the cache at slot cache_len
@@ -696,9 +699,6 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     unsigned kslot = 0;
     unsigned long long best = 0ull;
     embed_row(a, tok, m.xs);
-    // attention blocks stage layer 0's cached K/V rows (later layers: at the end of the layer
-    // before, off the critical path of the QKV phase)
-    if (attn_block) attention_prefetch<D>(a, 0, blockIdx.x, awork, cache_len, total_len);
     // One loop over the projection jobs (j = 4 l + {QKV, O, gate-up, down}, then the lm head)
     // with the phase-specific values selected at run time: the input / prologue / GEMV code
     // exists once in the kernel instead of once per phase, which keeps the instruction
@@ -709,6 +709,10 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     for (int j = 0; j <= 4 * a.L; ++j) {
         const int l = j >> 2, p = j & 3;
         const bool lm = j == 4 * a.L;
+        // attention blocks stage the layer's cached K/V rows, norm weights and RoPE rows
+        // before its QKV phase (right after the previous layer's down projection): fixed for
+        // this token, so the copies overlap the waits and the projection
+        if (p == 0 && !lm && attn_block) attention_prefetch<D>(a, l, blockIdx.x, awork, cache_len, total_len);
         const __half* norm = nullptr;
         if (lm) norm = a.out_norm;
         else if (p == 0) norm = a.layers[l].in_norm;
@@ -732,8 +736,6 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
         if (p == 0 && !lm && attn_block &&
             !attention_head<D>(a, m, l, blockIdx.x, awork, cache_len, total_len, t_out, vtag(a, 5 * l + 2)))
             return;
-        // the next layer's cache rows are fixed for this token and the staging area is free
-        if (p == 3 && attn_block && l + 1 < a.L) attention_prefetch<D>(a, l + 1, blockIdx.x, awork, cache_len, total_len);
     }
     // block first-max, then the last block to finish picks the token
     for (int o = 16; o > 0; o >>= 1) {
