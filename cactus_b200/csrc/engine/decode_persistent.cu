@@ -228,7 +228,7 @@ __device__ __forceinline__ void load_vec(const Cs& m, const __half* src, int K, 
     cbar();
 }
 
-constexpr int kMaxR = 4;  // 16-byte chunks of a tagged vector a consumer thread has in flight
+constexpr int kMaxR = 3;  // 16-byte chunks of a tagged vector a consumer thread has in flight
 
 // Stages K tagged fp16 activations (K % 4 == 0) into xs (with `transposed`, also the
 // lane-major copy xsT) once every word carries `tag`: each thread issues the loads of up to
@@ -390,6 +390,9 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
 // chain over the groups in order, times the activation scale -> fp16) + epilogue.
 // Outputs go to `out` as tagged words (`tag_out`; the residual read polls for `tag_res`),
 // the lm head's logits to `lm_out` as plain fp16.
+// CPG: 16-byte chunks per quantisation group (G / 16), a compile-time constant so the dot
+// loop is unrolled for exactly the group's chunks.
+template <int CPG>
 __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const Cs& m, uint8_t* ring, uint64_t* full,
                                          uint64_t* empty, unsigned& kslot, uint32_t* out, __half* lm_out,
                                          unsigned tag_out, unsigned tag_res, unsigned long long& best) {
@@ -399,15 +402,16 @@ __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const C
     rows_of(jw.N, blockIdx.x, gridDim.x, r0, r1);
     // group sums / scales of row r at [r * gst, r * gst + ng): gst keeps rows 16-byte aligned
     // and puts consecutive rows in different banks for the 16-byte loads of the chain
-    const int K = jw.K, ng = K / a.G, spr = rows_per_slot(a.slot_w, K), cpg = a.G / 16, gst = ((ng + 3) & ~3) + 4;
+    constexpr int G = CPG * 16;
+    const int K = jw.K, ng = K / G, spr = rows_per_slot(a.slot_w, K), gst = ((ng + 3) & ~3) + 4;
     // thread -> (row, group): the group is fixed for the whole job (so its activation chunks
     // stay in registers) and a round covers rpr rows
     const int rpr = kPC / ng, g = tid % ng, r_first = tid / ng;
     const bool tactive = r_first < rpr;
-    int4 ar[kMaxCpg];
+    int4 ar[CPG];
 #pragma unroll
-    for (int c = 0; c < kMaxCpg; ++c)
-        ar[c] = (tactive && c < cpg) ? *reinterpret_cast<const int4*>(m.act + g * a.G + c * 16) : make_int4(0, 0, 0, 0);
+    for (int c = 0; c < CPG; ++c)
+        ar[c] = tactive ? *reinterpret_cast<const int4*>(m.act + g * G + c * 16) : make_int4(0, 0, 0, 0);
     const float as = *m.as;
     const int NS = a.nslots, sb = a.slot_w + a.slot_s;
     for (int r = r0; r < r1; r += spr, ++kslot) {
@@ -432,20 +436,18 @@ __device__ __forceinline__ bool gemv_job(const PArgs& a, int j, int epi, const C
         mbar_wait_bounded(&full[s], par);  // completed already: makes the copy visible to this thread
         const uint8_t* wsl = ring + (size_t)s * sb;
         const uint16_t* ssl = reinterpret_cast<const uint16_t*>(wsl + a.slot_w);
-        // exact int32 sum of each (row, group): cpg 16-byte chunks, 4 dp4a each
+        // exact int32 sum of each (row, group): CPG 16-byte chunks, 4 dp4a each
         if (tactive) {
             for (int rr = r_first; rr < rows; rr += rpr) {
-                const int4* wp = reinterpret_cast<const int4*>(wsl + (size_t)rr * K + g * a.G);
+                const int4* wp = reinterpret_cast<const int4*>(wsl + (size_t)rr * K + g * G);
                 int acc = 0;
 #pragma unroll
-                for (int c = 0; c < kMaxCpg; ++c) {
-                    if (c < cpg) {
-                        const int4 wv = wp[c];
-                        acc = dp4a_ss(ar[c].x, wv.x, acc);
-                        acc = dp4a_ss(ar[c].y, wv.y, acc);
-                        acc = dp4a_ss(ar[c].z, wv.z, acc);
-                        acc = dp4a_ss(ar[c].w, wv.w, acc);
-                    }
+                for (int c = 0; c < CPG; ++c) {
+                    const int4 wv = wp[c];
+                    acc = dp4a_ss(ar[c].x, wv.x, acc);
+                    acc = dp4a_ss(ar[c].y, wv.y, acc);
+                    acc = dp4a_ss(ar[c].z, wv.z, acc);
+                    acc = dp4a_ss(ar[c].w, wv.w, acc);
                 }
                 m.gsm[rr * gst + g] = acc;
                 m.gsf[rr * gst + g] = h2f_bits(ssl[rr * ng + g]);
@@ -651,7 +653,7 @@ __device__ __forceinline__ void embed_row(const PArgs& a, uint32_t tok, __half* 
     cbar();
 }
 
-template <int D>
+template <int D, int CPG>
 __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[64];
@@ -732,7 +734,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PArgs a) {
         uint32_t* out = lm ? nullptr : (p == 0 ? a.qkv : p == 2 ? a.gated : a.hidden);
         const unsigned t_out = vtag(a, 5 * l + (p == 0 ? 1 : p == 1 ? 3 : p == 2 ? 4 : 5));
         const unsigned t_res = vtag(a, 5 * l + (p == 1 ? 0 : 3));  // O / down: the residual's version
-        if (!gemv_job(a, j, epi, m, ring, full, empty, kslot, out, a.logits, t_out, t_res, best)) return;
+        if (!gemv_job<CPG>(a, j, epi, m, ring, full, empty, kslot, out, a.logits, t_out, t_res, best)) return;
         if (p == 0 && !lm && attn_block &&
             !attention_head<D>(a, m, l, blockIdx.x, awork, cache_len, total_len, t_out, vtag(a, 5 * l + 2)))
             return;
@@ -836,9 +838,17 @@ PPlan persistent_plan(PArgs& a, int num_sms, size_t smem_optin) {
 }
 
 cudaError_t launch_persistent_decode(const PArgs& a, const PPlan& p, cudaStream_t st) {
-    void (*k)(PArgs) = a.D == 64 ? decode_persistent_kernel<64> : decode_persistent_kernel<128>;
-    static size_t attr_set[2] = {0, 0};  // largest dynamic shared memory enabled per variant
-    size_t& done = attr_set[a.D == 64 ? 0 : 1];
+    // one instantiation per (head dim, chunks per group); persistent_plan admits G = 16 .. 128
+    using Kfn = void (*)(PArgs);
+    static const Kfn table[2][4] = {
+        {decode_persistent_kernel<64, 1>, decode_persistent_kernel<64, 2>, decode_persistent_kernel<64, 4>,
+         decode_persistent_kernel<64, 8>},
+        {decode_persistent_kernel<128, 1>, decode_persistent_kernel<128, 2>, decode_persistent_kernel<128, 4>,
+         decode_persistent_kernel<128, 8>}};
+    const int gi = a.G == 16 ? 0 : a.G == 32 ? 1 : a.G == 64 ? 2 : 3;
+    Kfn k = table[a.D == 64 ? 0 : 1][gi];
+    static size_t attr_set[2][4] = {};  // largest dynamic shared memory enabled per variant
+    size_t& done = attr_set[a.D == 64 ? 0 : 1][gi];
     if (p.smem > done) {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
         if (e != cudaSuccess) return e;
