@@ -184,15 +184,34 @@ __global__ void argmax_rows_kernel(const __half* __restrict__ logits, int V, uin
     __shared__ unsigned long long red[32];
     const int b = blockIdx.x;
     const __half* lg = logits + (size_t)b * V;
+    // (value, ~index) keys: the maximum key is the first maximum whatever the scan order
+    auto key = [](__half h, int i) -> unsigned long long {
+        const float v = h2f(h);
+        if (v != v) return 0ull;
+        unsigned u = __float_as_uint(v);
+        u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        return ((unsigned long long)u << 32) | (0xFFFFFFFFu - (unsigned)i);
+    };
     unsigned long long best = 0ull;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = h2f(lg[i]);
-        unsigned long long k = 0ull;
-        if (v == v) {
-            unsigned u = __float_as_uint(v);
-            u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-            k = ((unsigned long long)u << 32) | (0xFFFFFFFFu - (unsigned)i);
+    int i0 = 0;
+    if ((reinterpret_cast<uintptr_t>(lg) & 15) == 0) {
+        // 16-byte loads of 8 logits, four in flight per thread (a vocabulary row is up to 512 KB)
+        const int n8 = V / 8;
+        const int4* l8 = reinterpret_cast<const int4*>(lg);
+#pragma unroll 4
+        for (int c = threadIdx.x; c < n8; c += blockDim.x) {
+            const int4 q = __ldg(l8 + c);
+            const __half* h = reinterpret_cast<const __half*>(&q);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const unsigned long long k = key(h[e], 8 * c + e);
+                best = k > best ? k : best;
+            }
         }
+        i0 = n8 * 8;
+    }
+    for (int i = i0 + threadIdx.x; i < V; i += blockDim.x) {
+        const unsigned long long k = key(lg[i], i);
         best = k > best ? k : best;
     }
     for (int o = 16; o > 0; o >>= 1) {

@@ -256,7 +256,25 @@ __global__ void argmax_kernel(const __half* __restrict__ logits, int V, uint32_t
     pdl_wait();
     __shared__ unsigned long long red[32];
     unsigned long long best = 0ull;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    int i0 = 0;
+    if ((reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
+        // 16-byte loads of 8 logits, four in flight per thread; the maximum key is the first
+        // maximum whatever the scan order
+        const int n8 = V / 8;
+        const int4* l8 = reinterpret_cast<const int4*>(logits);
+#pragma unroll 4
+        for (int c = threadIdx.x; c < n8; c += blockDim.x) {
+            const int4 q = __ldg(l8 + c);
+            const __half* h = reinterpret_cast<const __half*>(&q);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const unsigned long long k = argmax_key(h2f(h[e]), (unsigned)(8 * c + e));
+                best = k > best ? k : best;
+            }
+        }
+        i0 = n8 * 8;
+    }
+    for (int i = i0 + threadIdx.x; i < V; i += blockDim.x) {
         const unsigned long long k = argmax_key(h2f(logits[i]), (unsigned)i);
         best = k > best ? k : best;
     }
