@@ -265,6 +265,38 @@ CB_API int cactus_cuda_rms_norm_f16(const uint16_t* input, const uint16_t* weigh
     return check_launch("rms_norm_f16");
 }
 
+CB_API int cactus_cuda_conv1d_causal_depthwise_f16(const uint16_t* input, const uint16_t* weight, uint16_t* output,
+                                                   size_t N, size_t L, size_t C, size_t K, size_t dilation,
+                                                   void* stream) {
+    if (N == 0 || L == 0 || C == 0) return CB_OK;
+    if (K == 0 || dilation == 0) return fail(CB_ERR_ARG, "conv1d_causal_depthwise: kernel size and dilation must be >= 1");
+    if (N * L * C > (size_t)1 << 40 || L > kIntMax || C > kIntMax || K > kIntMax || (K - 1) * dilation > kIntMax)
+        return fail(CB_ERR_ARG, "conv1d_causal_depthwise: size too large");
+    cb::launch_conv1d_causal_depthwise(H(input), H(weight), H(output), (int)N, (int)L, (int)C, (int)K, (int)dilation,
+                                       S(stream));
+    return check_launch("conv1d_causal_depthwise_f16");
+}
+
+CB_API int cactus_cuda_conv1d_f16_k3(const uint16_t* input, const uint16_t* weight, uint16_t* output, size_t N,
+                                     size_t L, size_t C_in, size_t C_out, size_t stride, void* stream) {
+    if (N == 0 || L == 0 || C_out == 0) return CB_OK;
+    if (stride == 0) return fail(CB_ERR_ARG, "conv1d_k3: stride must be >= 1");
+    if (L > kIntMax || C_in > kIntMax || C_out > kIntMax || N * C_out * L > (size_t)1 << 40)
+        return fail(CB_ERR_ARG, "conv1d_k3: size too large");
+    cb::launch_conv1d_k3(H(input), H(weight), H(output), (int)N, (int)L, (int)C_in, (int)C_out, (int)stride, S(stream));
+    return check_launch("conv1d_f16_k3");
+}
+
+CB_API int cactus_cuda_layernorm_f16(const uint16_t* input, const uint16_t* weight, const uint16_t* bias,
+                                     uint16_t* output, size_t rows, size_t features, float eps, void* stream) {
+    if (rows == 0) return CB_OK;
+    if (features == 0 || features > (size_t)cb::layernorm_max_features())
+        return fail(CB_ERR_ARG, "layernorm: feature count out of range");
+    if (rows > kIntMax) return fail(CB_ERR_ARG, "layernorm: too many rows");
+    cb::launch_layernorm(H(input), H(weight), H(bias), H(output), (int)rows, (int)features, eps, S(stream));
+    return check_launch("layernorm_f16");
+}
+
 CB_API int cactus_cuda_rope_f16(const uint16_t* input, uint16_t* output, size_t batch_size, size_t seq_len,
                                 size_t num_heads, size_t head_dim, size_t start_pos, float theta, void* stream) {
     if (batch_size == 0 || seq_len == 0 || num_heads == 0) return CB_OK;

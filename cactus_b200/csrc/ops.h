@@ -44,6 +44,14 @@ constexpr int kGemmMinRows = 16;  // below this the GEMV is faster
 // ---- misc (misc.cu)
 int launch_quantize_act(const __half* x, int8_t* q, float* s, int M, int K, cudaStream_t st);
 int launch_rms_norm(const __half* x, const __half* w, __half* y, int rows, int dims, float eps, cudaStream_t st);
+// other families' kernels (conv_norm.cu)
+int launch_conv1d_causal_depthwise(const __half* x, const __half* w, __half* y, int N, int L, int C, int K, int dil,
+                                   cudaStream_t st);
+int launch_conv1d_k3(const __half* x, const __half* w, __half* y, int N, int L, int Cin, int Cout, int stride,
+                     cudaStream_t st);
+int layernorm_max_features();
+int launch_layernorm(const __half* x, const __half* w, const __half* b, __half* y, int rows, int F, float eps,
+                     cudaStream_t st);
 int launch_rope(const __half* in, __half* out, const __half* ct, const __half* stab, long long rows, int seq_len,
                 int heads, int head_dim, long long start_pos, cudaStream_t st);
 int launch_quantize_kv(const __half* src, int8_t* dst, float* scales, long long rows, int head_dim, int G,

@@ -72,6 +72,22 @@ CB_API int cactus_cuda_matmul_f16(const uint16_t* A, const uint16_t* B_transpose
 /* ---- RMSNorm: cactus_rms_norm_f16, kernel_attention.cpp:484-563 */
 CB_API int cactus_cuda_rms_norm_f16(const uint16_t* input, const uint16_t* weight, uint16_t* output,
                                     size_t batch_size, size_t dims, float eps, void* stream);
+/* ---- Causal depthwise conv1d (LFM2): cactus_conv1d_causal_depthwise_f16, kernel_conv.cpp:15-110.
+ *      input/output [N, L, C], weight [C, K]; output t of channel c sums weight[c][K-1-k] *
+ *      input[t - k*dilation][c] over taps k (positions before 0 are zero). */
+CB_API int cactus_cuda_conv1d_causal_depthwise_f16(const uint16_t* input, const uint16_t* weight, uint16_t* output,
+                                                   size_t N, size_t L, size_t C, size_t K, size_t dilation,
+                                                   void* stream);
+/* ---- Conv1d, kernel size 3, zero padding 1 (Whisper front end): cactus_conv1d_f16_k3,
+ *      kernel_conv.cpp:112-227. input [N, C_in, L], weight [C_out, C_in, 3],
+ *      output [N, C_out, (L - 1) / stride + 1]. */
+CB_API int cactus_cuda_conv1d_f16_k3(const uint16_t* input, const uint16_t* weight, uint16_t* output, size_t N,
+                                     size_t L, size_t C_in, size_t C_out, size_t stride, void* stream);
+/* ---- LayerNorm over the last dimension, fp16 in / out: compute_layernorm_node,
+ *      graph_ops_nn.cpp:373-457. input/output [rows, features], weight and bias [features];
+ *      features up to 14528 (shared-memory staging of the row). */
+CB_API int cactus_cuda_layernorm_f16(const uint16_t* input, const uint16_t* weight, const uint16_t* bias,
+                                     uint16_t* output, size_t rows, size_t features, float eps, void* stream);
 /* ---- RoPE (NeoX half rotation, fp16 cos/sin tables): cactus_rope_f16, kernel_attention.cpp:565-676.
  *      input/output [B, S, H, D]; position of token s is start_pos + s. */
 CB_API int cactus_cuda_rope_f16(const uint16_t* input, uint16_t* output, size_t batch_size,

@@ -72,6 +72,9 @@ def lib():
             "ref_fp16_to_int8": (None, [P, P, Z, F]),
             "ref_fp16_max_abs": (F, [P, Z]),
             "ref_rms_norm": (None, [P, P, P, Z, Z, F]),
+            "ref_conv1d_causal_depthwise": (None, [P, P, P, Z, Z, Z, Z, Z]),
+            "ref_conv1d_k3": (None, [P, P, P, Z, Z, Z, Z, Z]),
+            "ref_layernorm": (I, [P, P, P, P, Z, Z, F]),
             "ref_rope": (None, [P, P, Z, Z, Z, Z, Z, F]),
             "ref_softmax": (None, [P, P, Z, Z, Z]),
             "ref_silu": (None, [P, P, Z]),
@@ -161,6 +164,31 @@ def rms_norm(x, w, eps):
     x = _h(x)
     y = np.empty_like(x)
     lib().ref_rms_norm(_p(x), _p(_h(w)), _p(y), x.shape[0], x.shape[1], eps)
+    return y
+
+
+def conv1d_causal_depthwise(x, w, dilation=1):
+    x, w = _h(x), _h(w)
+    N, L, C = x.shape
+    y = np.empty_like(x)
+    lib().ref_conv1d_causal_depthwise(_p(x), _p(w), _p(y), N, L, C, w.shape[1], dilation)
+    return y
+
+
+def conv1d_k3(x, w, stride=1):
+    x, w = _h(x), _h(w)
+    N, Cin, L = x.shape
+    y = np.empty((N, w.shape[0], (L - 1) // stride + 1), np.float16)
+    lib().ref_conv1d_k3(_p(x), _p(w), _p(y), N, L, Cin, w.shape[0], stride)
+    return y
+
+
+def layernorm(x, w, b, eps):
+    """The reference's LAYERNORM graph node, run through a one-node CactusGraph."""
+    x = _h(x)
+    y = np.empty_like(x)
+    if lib().ref_layernorm(_p(x), _p(_h(w)), _p(_h(b)), _p(y), x.shape[0], x.shape[1], eps) != 0:
+        raise RuntimeError(lib().ref_last_error().decode())
     return y
 
 

@@ -172,6 +172,39 @@ float ref_fp16_max_abs(const uint16_t* src, size_t count) { return cactus_fp16_m
 void ref_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t rows, size_t dims, float eps) {
     cactus_rms_norm_f16(HP(x), HP(w), HW(y), rows, dims, eps);
 }
+void ref_conv1d_causal_depthwise(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t N, size_t L, size_t C,
+                                 size_t K, size_t dil) {
+    cactus_conv1d_causal_depthwise_f16(HP(x), HP(w), HW(y), N, L, C, K, dil);
+}
+void ref_conv1d_k3(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t N, size_t L, size_t Cin, size_t Cout,
+                   size_t stride) {
+    cactus_conv1d_f16_k3(HP(x), HP(w), HW(y), N, L, Cin, Cout, stride);
+}
+// The reference's layernorm is a graph node (compute_layernorm_node): one-node graph, fp16 in / out.
+int ref_layernorm(const uint16_t* x, const uint16_t* w, const uint16_t* b, uint16_t* y, size_t rows, size_t F,
+                  float eps) {
+    try {
+        CactusGraph g;
+        const size_t xi = g.input({rows, F}, Precision::FP16);
+        const size_t wi = g.input({F}, Precision::FP16);
+        const size_t bi = g.input({F}, Precision::FP16);
+        const size_t o = g.layernorm(xi, wi, bi, eps);
+        g.set_input(xi, x, Precision::FP16);
+        g.set_input(wi, w, Precision::FP16);
+        g.set_input(bi, b, Precision::FP16);
+        g.execute();
+        const auto& buf = g.get_output_buffer(o);
+        if (buf.precision != Precision::FP16 || buf.total_size != rows * F) {
+            g_err = "layernorm: unexpected output buffer";
+            return -1;
+        }
+        std::memcpy(y, g.get_output(o), rows * F * 2);
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
 void ref_rope(const uint16_t* x, uint16_t* y, size_t B, size_t S, size_t H, size_t D, size_t start, float theta) {
     cactus_rope_f16(HP(x), HW(y), B, S, H, D, start, theta);
 }

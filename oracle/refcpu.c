@@ -676,3 +676,82 @@ void ref_quantize_weights_int4(const float* w, uint8_t* packed, uint16_t* scales
         }
     }
 }
+
+/* ---------------------------------------------------------------- other families' kernels */
+/* cactus_conv1d_causal_depthwise_f16 (kernel_conv.cpp:15-110): input / output [N, L, C],
+ * weight [C, K] applied reversed (tap k reads x[t - k*dilation], zero before t = 0). Four
+ * fp32 lane accumulators take the taps of each 8-block (lane j: taps k+j, then k+4+j), the
+ * lanes fold as vaddvq_f32 ((l0 + l1) + (l2 + l3)), and the taps past the last 8-block are
+ * added one by one (contracted), skipping positions before the sequence start. */
+void ref_conv1d_causal_depthwise_f16(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t N, size_t L, size_t C,
+                                     size_t K, size_t dil) {
+    for (size_t n = 0; n < N; ++n)
+        for (size_t c = 0; c < C; ++c)
+            for (size_t t = 0; t < L; ++t) {
+                const uint16_t* xb = x + n * L * C;
+                float lane[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                size_t k = 0;
+                for (; k + 8 <= K; k += 8)
+                    for (int half = 0; half < 2; ++half)
+                        for (int j = 0; j < 4; ++j) {
+                            const size_t kk = k + 4 * half + j;
+                            const long long a = (long long)t - (long long)(kk * dil);
+                            const float xv = a >= 0 ? h2f(xb[(size_t)a * C + c]) : 0.0f;
+                            lane[j] = fmaf(xv, h2f(w[c * K + (K - 1 - kk)]), lane[j]);
+                        }
+                float acc = (lane[0] + lane[1]) + (lane[2] + lane[3]);
+                for (; k < K; ++k) {
+                    const long long a = (long long)t - (long long)(k * dil);
+                    if (a >= 0) acc = fmaf(h2f(w[c * K + (K - 1 - k)]), h2f(xb[(size_t)a * C + c]), acc);
+                }
+                y[n * L * C + t * C + c] = f2h(acc);
+            }
+}
+
+/* cactus_conv1d_f16_k3 (kernel_conv.cpp:112-227): input [N, C_in, L], weight [C_out, C_in, 3],
+ * output [N, C_out, (L - 1) / stride + 1], zero padding of one on both sides. Three fp32 lane
+ * chains (taps t-1, t, t+1) run over the input channels in order; the fold is
+ * (l0 + l2) + (l1 + l3) with lane 3 zero. */
+void ref_conv1d_f16_k3(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t N, size_t L, size_t Cin, size_t Cout,
+                       size_t stride) {
+    const size_t out_len = (L - 1) / stride + 1;
+    for (size_t n = 0; n < N; ++n)
+        for (size_t oc = 0; oc < Cout; ++oc)
+            for (size_t o = 0; o < out_len; ++o) {
+                const long long t = (long long)(o * stride);
+                float lane[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                for (size_t ic = 0; ic < Cin; ++ic) {
+                    const uint16_t* xc = x + (n * Cin + ic) * L;
+                    const uint16_t* wc = w + (oc * Cin + ic) * 3;
+                    const float xm = t - 1 >= 0 ? h2f(xc[t - 1]) : 0.0f;
+                    const float x0 = h2f(xc[t]);
+                    const float xp = t + 1 < (long long)L ? h2f(xc[t + 1]) : 0.0f;
+                    lane[0] = fmaf(xm, h2f(wc[0]), lane[0]);
+                    lane[1] = fmaf(x0, h2f(wc[1]), lane[1]);
+                    lane[2] = fmaf(xp, h2f(wc[2]), lane[2]);
+                    lane[3] = fmaf(0.0f, 0.0f, lane[3]);
+                }
+                y[(n * Cout + oc) * out_len + o] = f2h((lane[0] + lane[2]) + (lane[1] + lane[3]));
+            }
+}
+
+/* compute_layernorm_node (graph_ops_nn.cpp:373-457), fp16 input / weight / bias / output:
+ * in-order fp32 sums for the mean and the variance (diff*diff contracted), divided by the
+ * feature count, inv = 1 / sqrtf(var + eps), y = fp16(fma((x - mean) * inv, w, b)). */
+void ref_layernorm_f16(const uint16_t* x, const uint16_t* w, const uint16_t* b, uint16_t* y, size_t rows, size_t F,
+                       float eps) {
+    for (size_t r = 0; r < rows; ++r) {
+        const uint16_t* xr = x + r * F;
+        float mean = 0.0f;
+        for (size_t i = 0; i < F; ++i) mean += h2f(xr[i]);
+        mean /= (float)F;
+        float var = 0.0f;
+        for (size_t i = 0; i < F; ++i) {
+            const float d = h2f(xr[i]) - mean;
+            var = fmaf(d, d, var);
+        }
+        var /= (float)F;
+        const float inv = 1.0f / sqrtf(var + eps);
+        for (size_t i = 0; i < F; ++i) y[r * F + i] = f2h(fmaf((h2f(xr[i]) - mean) * inv, h2f(w[i]), h2f(b[i])));
+    }
+}

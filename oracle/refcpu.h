@@ -101,7 +101,16 @@ void ref_unpack_int4(const uint8_t* packed, int8_t* out, size_t count);
 void ref_quantize_weights_int8(const float* w, int8_t* q, uint16_t* scales, size_t N, size_t K, size_t G);
 void ref_quantize_weights_int4(const float* w, uint8_t* packed, uint16_t* scales, size_t N, size_t K, size_t G);
 
+/* other families' kernels: LFM2 causal depthwise conv, Whisper conv1d k=3, layernorm */
+void ref_conv1d_causal_depthwise_f16(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t N, size_t L, size_t C,
+                                     size_t K, size_t dil);
+void ref_conv1d_f16_k3(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t N, size_t L, size_t Cin, size_t Cout,
+                       size_t stride);
+void ref_layernorm_f16(const uint16_t* x, const uint16_t* w, const uint16_t* b, uint16_t* y, size_t rows, size_t F,
+                       float eps);
+
 #ifdef __cplusplus
 }
 #endif
 #endif
+

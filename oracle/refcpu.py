@@ -52,6 +52,9 @@ def _declare(L):
         "ref_matmul_int4": (None, [P, P, P, P, P, Z, Z, Z, Z]),
         "ref_matmul_f16": (None, [P, P, P, Z, Z, Z]),
         "ref_rms_norm_f16": (None, [P, P, P, Z, Z, F]),
+        "ref_conv1d_causal_depthwise_f16": (None, [P, P, P, Z, Z, Z, Z, Z]),
+        "ref_conv1d_f16_k3": (None, [P, P, P, Z, Z, Z, Z, Z]),
+        "ref_layernorm_f16": (None, [P, P, P, P, Z, Z, F]),
         "ref_rope_tables": (None, [P, P, Z, Z, F]),
         "ref_rope_f16": (None, [P, P, Z, Z, Z, Z, Z, F]),
         "ref_attention_f16": (None, [P, P, P, P, Z, Z, Z, Z, Z, Z, F, Z, Z, I]),
@@ -144,6 +147,35 @@ def rms_norm(x, w, eps):
     rows, dims = x.shape
     y = np.empty_like(x)
     lib().ref_rms_norm_f16(_p(x), _p(w), _p(y), rows, dims, eps)
+    return y
+
+
+def conv1d_causal_depthwise(x, w, dilation=1):
+    """cactus_conv1d_causal_depthwise_f16: x [N, L, C], w [C, K] -> [N, L, C] (kernel_conv.cpp:15-110)."""
+    x, w = _c(x, np.float16), _c(w, np.float16)
+    N, L, C = x.shape
+    y = np.empty_like(x)
+    lib().ref_conv1d_causal_depthwise_f16(_p(x), _p(w), _p(y), N, L, C, w.shape[1], dilation)
+    return y
+
+
+def conv1d_k3(x, w, stride=1):
+    """cactus_conv1d_f16_k3: x [N, C_in, L], w [C_out, C_in, 3] -> [N, C_out, (L-1)//stride + 1]
+    (kernel_conv.cpp:112-227)."""
+    x, w = _c(x, np.float16), _c(w, np.float16)
+    N, Cin, L = x.shape
+    Cout = w.shape[0]
+    y = np.empty((N, Cout, (L - 1) // stride + 1), np.float16)
+    lib().ref_conv1d_f16_k3(_p(x), _p(w), _p(y), N, L, Cin, Cout, stride)
+    return y
+
+
+def layernorm(x, w, b, eps):
+    """compute_layernorm_node with fp16 tensors (graph_ops_nn.cpp:373-457): x [rows, F]."""
+    x, w, b = _c(x, np.float16), _c(w, np.float16), _c(b, np.float16)
+    rows, F = x.shape
+    y = np.empty_like(x)
+    lib().ref_layernorm_f16(_p(x), _p(w), _p(b), _p(y), rows, F, eps)
     return y
 
 

@@ -148,6 +148,46 @@ def test_rms_norm_bit_exact(L, ref, rows, dims):
     assert same_bits(host(y, np.float16), ref.rms_norm(x, w, 1e-6))
 
 
+# ----------------------------------------------------------------------------- other families' kernels
+@pytest.mark.parametrize("N,Lx,C,K,dil", [(1, 37, 64, 3, 1), (2, 20, 48, 4, 2), (1, 50, 32, 11, 1), (1, 9, 16, 8, 1),
+                                          (1, 64, 40, 17, 3), (3, 1, 5, 3, 1), (1, 300, 1024, 3, 1)])
+def test_conv1d_causal_depthwise_bit_exact(L, ref, N, Lx, C, K, dil):
+    """LFM2's causal depthwise conv (kernel_conv.cpp:15-110): 8-tap lane blocks, tails, dilation."""
+    rng = np.random.default_rng(N * 1000 + Lx + C + K)
+    x, w = f16(rng, (N, Lx, C)), f16(rng, (C, K), 0.5)
+    y = empty((N, Lx, C), np.float16)
+    cb.check(L.cactus_cuda_conv1d_causal_depthwise_f16(ptr(dev(x)), ptr(dev(w)), ptr(y), N, Lx, C, K, dil, None))
+    assert same_bits(host(y, np.float16), ref.conv1d_causal_depthwise(x, w, dil))
+
+
+@pytest.mark.parametrize("N,Cin,Lx,Cout,stride", [(1, 80, 30, 24, 1), (2, 17, 9, 8, 2), (1, 5, 1, 3, 1),
+                                                  (1, 40, 33, 16, 2), (1, 80, 3000, 64, 1), (1, 384, 200, 96, 2)])
+def test_conv1d_k3_bit_exact(L, ref, N, Cin, Lx, Cout, stride):
+    """Whisper's front-end conv1d, kernel 3, padding 1 (kernel_conv.cpp:112-227), strides 1 and 2."""
+    rng = np.random.default_rng(N + Cin + Lx + Cout)
+    x, w = f16(rng, (N, Cin, Lx)), f16(rng, (Cout, Cin, 3), 0.3)
+    out_len = (Lx - 1) // stride + 1
+    y = empty((N, Cout, out_len), np.float16)
+    cb.check(L.cactus_cuda_conv1d_f16_k3(ptr(dev(x)), ptr(dev(w)), ptr(y), N, Lx, Cin, Cout, stride, None))
+    assert same_bits(host(y, np.float16), ref.conv1d_k3(x, w, stride))
+
+
+@pytest.mark.parametrize("rows,F", [(3, 768), (5, 384), (1, 1000), (2, 7), (70, 1280), (1, 14528)])
+def test_layernorm_bit_exact(L, ref, rows, F):
+    """compute_layernorm_node (graph_ops_nn.cpp:373-457): in-order mean and variance sums."""
+    rng = np.random.default_rng(rows + F)
+    x, w, b = f16(rng, (rows, F), 2.0), f16(rng, (F,)), f16(rng, (F,), 0.1)
+    y = empty((rows, F), np.float16)
+    cb.check(L.cactus_cuda_layernorm_f16(ptr(dev(x)), ptr(dev(w)), ptr(dev(b)), ptr(y), rows, F, 1e-5, None))
+    assert same_bits(host(y, np.float16), ref.layernorm(x, w, b, 1e-5))
+
+
+def test_layernorm_rejects_oversized_rows(L):
+    y = empty((1, 16), np.float16)
+    assert L.cactus_cuda_layernorm_f16(ptr(y), ptr(y), ptr(y), ptr(y), 1, 14529, 1e-5, None) != 0
+    assert b"feature count" in L.cactus_cuda_last_error()
+
+
 @pytest.mark.parametrize("B,S,H,D,start,theta", [(1, 7, 3, 128, 100, 1e6), (2, 5, 2, 64, 0, 5e5),
                                                   (1, 3, 1, 12, 9, 1e4), (1, 1, 8, 256, 4095, 1e4)])
 def test_rope_bit_exact(L, ref, B, S, H, D, start, theta):

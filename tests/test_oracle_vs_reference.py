@@ -210,3 +210,32 @@ def test_engine_sliding_window_matches(tmp_path):
         assert ta == tb
     R.set_chunk_pool(0)
     ref.close()
+
+
+@pytest.mark.parametrize("N,Lx,C,K,dil", [(1, 37, 64, 3, 1), (2, 20, 48, 4, 2), (1, 50, 32, 11, 1), (1, 64, 40, 17, 3)])
+def test_conv1d_causal_depthwise(N, Lx, C, K, dil):
+    rng = np.random.default_rng(N + Lx + C + K)
+    x, w = h(rng, N, Lx, C), h(rng, C, K, scale=0.5)
+    same(R.conv1d_causal_depthwise(x, w, dil), RF.conv1d_causal_depthwise(x, w, dil))
+
+
+@pytest.mark.parametrize("N,Cin,Lx,Cout,stride", [(1, 80, 30, 24, 1), (2, 17, 9, 8, 2), (1, 5, 1, 3, 1)])
+def test_conv1d_k3(N, Cin, Lx, Cout, stride):
+    rng = np.random.default_rng(N + Cin + Lx + Cout)
+    x, w = h(rng, N, Cin, Lx), h(rng, Cout, Cin, 3, scale=0.3)
+    same(R.conv1d_k3(x, w, stride), RF.conv1d_k3(x, w, stride))
+
+
+@pytest.mark.parametrize("rows,F", [(3, 768), (5, 384), (1, 1000), (2, 7)])
+def test_layernorm(rows, F):
+    """compute_layernorm_node through a one-node graph of the reference. The restatement fuses
+    `variance += diff * diff` as the reference's compilers contract it (clang, -ffp-contract=on).
+    The x86 g++ build used here leaves that loop-carried accumulation unfused whatever the
+    contraction flags, so a variance can differ in its last bit and, rarely, an output by one
+    fp16 unit in the last place: everything else must be identical."""
+    rng = np.random.default_rng(rows + F)
+    x, w, b = h(rng, rows, F, scale=2.0), h(rng, F), h(rng, F, scale=0.1)
+    a, r = R.layernorm(x, w, b, 1e-5), RF.layernorm(x, w, b, 1e-5)
+    ai, ri = a.view(np.int16).astype(np.int32), r.view(np.int16).astype(np.int32)
+    assert np.abs(ai - ri).max() <= 1
+    assert np.count_nonzero(ai != ri) <= max(1, a.size // 1000)
