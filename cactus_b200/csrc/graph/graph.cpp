@@ -49,6 +49,9 @@ const char* op_name(OpType t) {
         case OpType::RESHAPE: return "RESHAPE";
         case OpType::EMBEDDING: return "EMBEDDING";
         case OpType::RMS_NORM: return "RMS_NORM";
+        case OpType::LAYERNORM: return "LAYERNORM";
+        case OpType::CONV1D_CAUSAL: return "CONV1D_CAUSAL";
+        case OpType::CONV1D_K3: return "CONV1D_K3";
         case OpType::ROPE: return "ROPE";
         case OpType::SOFTMAX: return "SOFTMAX";
         case OpType::ATTENTION: return "ATTENTION";
@@ -275,6 +278,32 @@ size_t CactusGraph::embedding(size_t table, size_t indices) {
     OpParams p;
     p.output_precision = Precision::FP16;
     return add_node(OpType::EMBEDDING, {table, indices}, out, p);
+}
+
+size_t CactusGraph::layernorm(size_t in, size_t weight, size_t bias, float epsilon) {
+    OpParams p;
+    p.epsilon = epsilon;
+    return add_node(OpType::LAYERNORM, {in, weight, bias}, {}, p);
+}
+
+size_t CactusGraph::conv1d_causal(size_t in, size_t weight, size_t, size_t dilation) {
+    OpParams p;
+    p.dilation = dilation;
+    return add_node(OpType::CONV1D_CAUSAL, {in, weight}, {}, p);
+}
+
+size_t CactusGraph::conv1d_k3(size_t in, size_t weight, size_t stride) {  // graph_builder.cpp:323-345
+    const BufferDesc& x = get_output_buffer(in);
+    const BufferDesc& w = get_output_buffer(weight);
+    if (x.shape.size() != 3) throw std::runtime_error("conv1d_k3 expects N,C,L");
+    if (w.shape.size() != 3) throw std::runtime_error("weight must be [C_out,C_in,3]");
+    if (w.shape[1] != x.shape[1]) throw std::runtime_error("C_in mismatch in conv1d_k3");
+    if (w.shape[2] != 3) throw std::runtime_error("K=3 expected in conv1d_k3");
+    if (stride == 0) throw std::runtime_error("conv1d_k3: stride must be >= 1");
+    OpParams p;
+    p.stride = stride;
+    p.output_precision = x.precision;
+    return add_node(OpType::CONV1D_K3, {in, weight}, {x.shape[0], w.shape[0], (x.shape[2] - 1) / stride + 1}, p);
 }
 
 size_t CactusGraph::rms_norm(size_t in, size_t weight, float epsilon) {
@@ -613,6 +642,45 @@ void CactusGraph::compute_node(GraphNode& node) {
             need(x, Precision::FP16, "RMS normalization only supports FP16 precision");
             kck(cactus_cuda_rms_norm_f16(u16(x.device_data), u16(w.device_data), u16(o), x.shape[0], x.shape[1],
                                          node.params.epsilon, sv), "rms_norm");
+            break;
+        }
+        case OpType::LAYERNORM: {  // graph_ops_nn.cpp:373-457
+            BufferDesc& x = in(0);
+            BufferDesc& w = in(1);
+            BufferDesc& b = in(2);
+            if (x.shape.empty()) throw std::runtime_error("LayerNorm requires non-empty input tensor");
+            need(x, Precision::FP16, "LayerNorm on the B200 backend supports FP16 input");
+            need(w, Precision::FP16, "LayerNorm on the B200 backend supports FP16 weight");
+            need(b, Precision::FP16, "LayerNorm on the B200 backend supports FP16 bias");
+            const size_t F = x.shape.back();
+            kck(cactus_cuda_layernorm_f16(u16(x.device_data), u16(w.device_data), u16(b.device_data), u16(o),
+                                          x.total_size / F, F, node.params.epsilon, sv),
+                "layernorm");
+            break;
+        }
+        case OpType::CONV1D_CAUSAL: {  // graph_ops_nn.cpp:459-530
+            BufferDesc& x = in(0);
+            BufferDesc& w = in(1);
+            if (x.shape.size() != 3) throw std::runtime_error("Causal conv requires 3D input [batch, seq_len, in_channels]");
+            if (w.shape.size() != 3) throw std::runtime_error("Weight must be 3D");
+            if (w.shape[1] != 1 || w.shape[0] != x.shape[2])
+                throw std::runtime_error("Only depthwise causal convolution is supported currently");
+            if (node.params.dilation < 1) throw std::runtime_error("dilation must be >= 1");
+            need(x, Precision::FP16, "Depthwise causal conv on the B200 backend supports FP16 input");
+            need(w, Precision::FP16, "Depthwise causal conv on the B200 backend supports FP16 weights");
+            kck(cactus_cuda_conv1d_causal_depthwise_f16(u16(x.device_data), u16(w.device_data), u16(o), x.shape[0],
+                                                        x.shape[1], x.shape[2], w.shape[2], node.params.dilation, sv),
+                "conv1d_causal");
+            break;
+        }
+        case OpType::CONV1D_K3: {  // graph_ops_nn.cpp:532-580
+            BufferDesc& x = in(0);
+            BufferDesc& w = in(1);
+            need(x, Precision::FP16, "Conv1d_k3 on the B200 backend supports FP16 input");
+            need(w, Precision::FP16, "Conv1d_k3 on the B200 backend supports FP16 weights");
+            kck(cactus_cuda_conv1d_f16_k3(u16(x.device_data), u16(w.device_data), u16(o), x.shape[0], x.shape[2],
+                                          x.shape[1], w.shape[0], node.params.stride, sv),
+                "conv1d_k3");
             break;
         }
         case OpType::ROPE: {  // graph_ops_nn.cpp:255-282

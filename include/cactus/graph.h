@@ -101,6 +101,8 @@ struct OpParams {
     size_t cache_seq_len = 0;
     size_t num_kv_heads = 0;
     size_t head_dim = 0;
+    size_t dilation = 1;  // CONV1D_CAUSAL
+    size_t stride = 1;    // CONV1D_K3
 };
 
 struct GraphNode {
@@ -142,6 +144,12 @@ public:
     size_t embedding(size_t embedding_tensor, size_t indices);
 
     size_t rms_norm(size_t input, size_t weight, float epsilon = 1e-5f);
+    // fp16 input [rows, features], fp16 weight and bias [features] (graph_ops_nn.cpp:373-457)
+    size_t layernorm(size_t input, size_t weight, size_t bias, float epsilon = 1e-5f);
+    // depthwise causal conv: fp16 input [N, L, C], fp16 weight [C, 1, K] (graph_ops_nn.cpp:459-530)
+    size_t conv1d_causal(size_t input, size_t weight, size_t kernel_size, size_t dilation = 1);
+    // kernel-3 conv, padding 1: fp16 input [N, C_in, L], fp16 weight [C_out, C_in, 3] (graph_ops_nn.cpp:532-580)
+    size_t conv1d_k3(size_t input, size_t weight, size_t stride);
     size_t rope(size_t input, float theta, size_t position_offset = 0, ComputeBackend backend = ComputeBackend::CPU);
     size_t softmax(size_t input, int axis = -1);
     size_t attention(size_t query, size_t key, size_t value, float scale, bool is_causal = true,

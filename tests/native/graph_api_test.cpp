@@ -271,6 +271,33 @@ void block(const std::string& dir) {
     g.soft_reset();
     report("soft_reset_keeps_weights", g.get_node_count() == 6 && g.mmap_weights(dir + "/wq.weights") == wq);
 }
+// LFM2 / Whisper / encoder ops: causal depthwise conv, conv1d k=3 (stride 2), layernorm; the
+// inputs come from the Python side, the outputs are compared there with the oracle
+void families(const std::string& dir) {
+    CactusGraph g;
+    const size_t N = 1, L = 20, C = 16, K = 4, Cin = 8, Lk = 12, Cout = 6, R = 3, F = 40;
+    auto in = [&](const std::vector<size_t>& shape, const std::string& name) {
+        size_t n = 1;
+        for (size_t d : shape) n *= d;
+        const size_t id = g.input(shape, Precision::FP16);
+        const std::vector<uint16_t> v = read_f16(dir + "/" + name, n);
+        g.set_input(id, v.data(), Precision::FP16);
+        return id;
+    };
+    const size_t xd = in({N, L, C}, "x_dw.bin"), wd = in({C, 1, K}, "w_dw.bin");
+    const size_t xk = in({N, Cin, Lk}, "x_k3.bin"), wk = in({Cout, Cin, 3}, "w_k3.bin");
+    const size_t xl = in({R, F}, "x_ln.bin"), wl = in({F}, "w_ln.bin"), bl = in({F}, "b_ln.bin");
+    const size_t dw = g.conv1d_causal(xd, wd, K, 2);
+    const size_t k3 = g.conv1d_k3(xk, wk, 2);
+    const size_t ln = g.layernorm(xl, wl, bl, 1e-5f);
+    g.execute();
+    report("families_shapes", g.get_output_buffer(dw).shape == std::vector<size_t>({N, L, C}) &&
+                                  g.get_output_buffer(k3).shape == std::vector<size_t>({N, Cout, (Lk - 1) / 2 + 1}) &&
+                                  g.get_output_buffer(ln).shape == std::vector<size_t>({R, F}));
+    dump(g, dw, dir + "/out_dw.bin");
+    dump(g, k3, dir + "/out_k3.bin");
+    dump(g, ln, dir + "/out_ln.bin");
+}
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -281,6 +308,7 @@ int main(int argc, char** argv) {
     try {
         known_answers(argv[1]);
         block(argv[1]);
+        families(argv[1]);
     } catch (const std::exception& e) {
         std::printf("FAIL exception: %s\n", e.what());
         return 1;

@@ -48,6 +48,15 @@ def test_graph_api(tmp_path):
     W.save_tensor(os.path.join(d, "emb_f16.weights"),
                   np.array([[1, 5, 9], [2, 6, 10], [3, 7, 11], [4, 8, 12]], np.float32), "FP16")
 
+    # inputs of the LFM2 / Whisper / encoder ops (native families())
+    x_dw, w_dw = rng.standard_normal((1, 20, 16)).astype(np.float16), (rng.standard_normal((16, 1, 4)) * 0.5).astype(np.float16)
+    x_k3, w_k3 = rng.standard_normal((1, 8, 12)).astype(np.float16), (rng.standard_normal((6, 8, 3)) * 0.3).astype(np.float16)
+    x_ln = (rng.standard_normal((3, 40)) * 2).astype(np.float16)
+    w_ln, b_ln = rng.standard_normal(40).astype(np.float16), (rng.standard_normal(40) * 0.1).astype(np.float16)
+    for name, arr in (("x_dw", x_dw), ("w_dw", w_dw), ("x_k3", x_k3), ("w_k3", w_k3), ("x_ln", x_ln), ("w_ln", w_ln),
+                      ("b_ln", b_ln)):
+        arr.tofile(os.path.join(d, f"{name}.bin"))
+
     exe = _build(d)
     r = subprocess.run([exe, d], capture_output=True, text=True, timeout=300)
     print(r.stdout)
@@ -78,5 +87,9 @@ def test_graph_api(tmp_path):
         g = got(name, np.float16, ref.shape)
         assert np.array_equal(g.view(np.uint16), ref.view(np.uint16)), name
     assert int(got("tok", np.uint32, (1,))[0]) == int(np.argmax(logits[M - 1].astype(np.float32)))
+    for name, ref in (("dw", R.conv1d_causal_depthwise(x_dw, w_dw.reshape(16, 4), 2)), ("k3", R.conv1d_k3(x_k3, w_k3, 2)),
+                      ("ln", R.layernorm(x_ln, w_ln, b_ln, 1e-5))):
+        g = got(name, np.float16, ref.shape)
+        assert np.array_equal(g.view(np.uint16), ref.view(np.uint16)), name
     prof = open(os.path.join(d, "profile.txt")).read()
     assert "MATMUL" in prof and "TOTAL" in prof
