@@ -30,7 +30,9 @@ __global__ void __launch_bounds__(128) attn_f16_kernel(const __half* __restrict_
     pdl_launch_dependents();
     pdl_wait();
     __shared__ float qs[4][kMaxHeadDim];
+    extern __shared__ __align__(16) __half vstage_all[];  // per warp: the block's 32 value rows [32][D]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __half* vstage = vstage_all + (size_t)warp * 32 * D;
     const long long item = (long long)blockIdx.x * 4 + warp;  // ((b*Hq + h)*S + q)
     if (item >= (long long)B * Hq * S) return;
     const int qp = (int)(item % S);
@@ -103,10 +105,28 @@ __global__ void __launch_bounds__(128) attn_f16_kernel(const __half* __restrict_
         float bsum = 0.0f;
         for (int qd = 0; qd < vec; qd += 4) bsum = __fadd_rn(bsum, __shfl_sync(0xffffffffu, quad, qd));
         for (int i = vec; i < bs; ++i) bsum = __fadd_rn(bsum, __shfl_sync(0xffffffffu, y, i));
+        // stage the block's value rows with the warp's loads (16 bytes a lane where the rows
+        // allow), so the in-order accumulation below reads shared memory instead of waiting
+        // on a global load per key
+        __syncwarp();
+        if ((D & 7) == 0 && (kv_row & 7) == 0 && (reinterpret_cast<uintptr_t>(Vb) & 15) == 0) {
+            const int cpr = D / 8;  // 16-byte chunks per row
+            for (int c = lane; c < bs * cpr; c += 32) {
+                const int i = c / cpr, j = c - i * cpr;
+                reinterpret_cast<int4*>(vstage + (size_t)i * D)[j] =
+                    __ldg(reinterpret_cast<const int4*>(Vb + (size_t)(b0 + i) * kv_row) + j);
+            }
+        } else {
+            for (int c = lane; c < bs * D; c += 32) {
+                const int i = c / D, d = c - i * D;
+                vstage[(size_t)i * D + d] = Vb[(size_t)(b0 + i) * kv_row + d];
+            }
+        }
+        __syncwarp();
         for (int i = 0; i < bs; ++i) {
             const float w = __shfl_sync(0xffffffffu, y, i);
             if (w == 0.0f) continue;
-            const __half* vr = Vb + (size_t)(b0 + i) * kv_row;
+            const __half* vr = vstage + (size_t)i * D;
             for (int t = 0; t < dpl; ++t)
                 if (lane + 32 * t < hda) acc[t] = fmaf(h2f(vr[lane + 32 * t]), w, acc[t]);
         }
@@ -367,8 +387,18 @@ int launch_attention_f16(const __half* q, const __half* k, const __half* v, __ha
                          int Hkv, int D, float scale, long long pos_off, long long window, int causal,
                          cudaStream_t st) {
     const long long items = (long long)B * Hq * S;
-    launch_k(attn_f16_kernel, dim3((unsigned)((items + 3) / 4)), dim3(128), 0, st, q, k, v, o, B, S, Skv, Hq, Hkv, D, scale, pos_off,
-                                                                 window, causal);
+    const size_t smem = (size_t)4 * 32 * D * sizeof(__half);  // per warp, one 32-key block of value rows
+    if (smem > 48 * 1024) {
+        static size_t enabled = 0;
+        if (smem > enabled) {
+            if (cudaFuncSetAttribute(attn_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                cudaSuccess)
+                return -1;
+            enabled = smem;
+        }
+    }
+    launch_k(attn_f16_kernel, dim3((unsigned)((items + 3) / 4)), dim3(128), smem, st, q, k, v, o, B, S, Skv, Hq, Hkv, D,
+             scale, pos_off, window, causal);
     return 0;
 }
 
