@@ -609,8 +609,13 @@ __device__ __forceinline__ bool attention_head(const PArgs& a, const Cs& m, int 
     }
     cbar();
     for (int d = tid; d < D; d += kPC) qs[d] = h2f(qr[d]);
+    cbar();
+    const __half o = attn_exact_core<D, kPC, kACH>(c, work, SyncConsumers{});
+    if (tid < D) st_tagged(a.attn + (size_t)h * D + tid, o, ta);
     // the first q head of each group appends the step's K/V to the cache at slot cache_len
-    // (c.Kc / c.Vc / c.ks / c.vs point at this kv head's row 0)
+    // (c.Kc / c.Vc / c.ks / c.vs point at this kv head's row 0). Only the next token reads
+    // that row (this token's attention takes the new key and value from shared memory), so
+    // the append runs after the output is published, off the critical path.
     if (h % grp == 0 && warp >= 2 && warp < 2 + 2 * nqg) {
         const int which = (warp - 2) / nqg, g = (warp - 2) % nqg;
         const int cnt = min(128, D - g * 128);
@@ -620,9 +625,6 @@ __device__ __forceinline__ bool attention_head(const PArgs& a, const Cs& m, int 
         float* sdst = const_cast<float*>(which ? c.vs : c.ks) + (size_t)row * c.sc_row + g;
         kv_quant_group_warp(src, cnt, dst, sdst);
     }
-    cbar();
-    const __half o = attn_exact_core<D, kPC, kACH>(c, work, SyncConsumers{});
-    if (tid < D) st_tagged(a.attn + (size_t)h * D + tid, o, ta);
     return true;
 }
 
